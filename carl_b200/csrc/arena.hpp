@@ -1,0 +1,46 @@
+// Host-side arena build: collision mesh -> device tables.
+//
+// Produces the same tables as the reference's ArenaMesh constructor
+// (jwmccarthy/CARL src/ArenaMesh.cu:15-125 with include/Arena/ObjLoader.cuh:91-126,
+// TriMesh.cuh:21-66, BroadPhaseGrid.cuh:12-78, EdgeInfo.cuh:61-125): OBJ vertices
+// read as (y, x, z), exact-bit vertex welding, unit face normals, a 48x48x10
+// uniform grid whose cells list every triangle whose (one-cell-dilated) AABB
+// overlaps them in ascending triangle order, and the signed dihedral angle of
+// every shared edge (2*pi on boundary edges).  Only the default arena path is
+// built (no native-metadata override), so the ball's per-cell triangle order is
+// the car's order.
+#pragma once
+
+#include <cstdint>
+#include <string>
+#include <vector>
+
+namespace cb {
+
+// Triangle flag bits (ArenaHost::triFlags).
+enum : int32_t {
+    TRI_ANALYTIC_PLANE = 1,  // floor, ceiling or flat side wall: skipped by car-vs-mesh SAT
+};
+
+struct ArenaHost
+{
+    std::vector<float> verts;       // [nVerts][3]
+    std::vector<int32_t> tris;      // [nTris][3] welded vertex ids
+    std::vector<float> normals;     // [nTris][3]
+    std::vector<float> edgeAngles;  // [nTris][3], edge i = (v_i, v_(i+1)%3)
+    std::vector<int32_t> triFlags;  // [nTris]
+    std::vector<int32_t> cellStart; // [NUM_CELLS + 1]
+    std::vector<int32_t> cellTris;  // [cellStart[NUM_CELLS]]
+    int32_t maxCellTris = 0;
+
+    int nVerts() const { return (int)verts.size() / 3; }
+    int nTris() const { return (int)tris.size() / 3; }
+};
+
+// Path of the arena mesh: $CARL_ARENA_OBJ if set, else `fallback`.
+std::string arenaObjPath(const std::string& fallback);
+
+// Builds the tables; returns an empty string on success, else the error.
+std::string buildArena(const std::string& objPath, ArenaHost& out);
+
+}  // namespace cb

@@ -1,0 +1,736 @@
+// carlb_env: one env on one CUDA device behind the C ABI of include/carlb.h.
+//
+// Host orchestration of an RL step (jwmccarthy/CARL python/carl.cu:312-370):
+//   copy actions -> fused tick kernel (frameskip ticks in one launch) ->
+//   rewards/dones -> transition state / obs -> auto-reset -> obs, state.
+// Everything is enqueued on the env's own non-blocking stream; the host keeps
+// the tick counter.  Errors are returned as carlb_status with a message; no
+// entry point exits the process.
+#include <dlfcn.h>
+
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/carlb.h"
+#include "arena.hpp"
+#include "envio.cuh"
+#include "tick.cuh"
+
+using namespace cb;
+
+namespace {
+
+thread_local std::string g_createError;
+
+std::string libraryDir()
+{
+    Dl_info info{};
+    if (dladdr(reinterpret_cast<void*>(&libraryDir), &info) && info.dli_fname)
+    {
+        std::string p = info.dli_fname;
+        const size_t slash = p.rfind('/');
+        return slash == std::string::npos ? std::string(".") : p.substr(0, slash);
+    }
+    return ".";
+}
+
+// Host arena tables, built once per process and path.
+std::shared_ptr<const ArenaHost> hostArena(const std::string& path, std::string& err)
+{
+    static std::mutex mu;
+    static std::map<std::string, std::shared_ptr<const ArenaHost>> cache;
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(path);
+    if (it != cache.end()) return it->second;
+    auto a = std::make_shared<ArenaHost>();
+    err = buildArena(path, *a);
+    if (!err.empty()) return nullptr;
+    cache[path] = a;
+    return a;
+}
+
+}  // namespace
+
+struct carlb_env
+{
+    carlb_config cfg{};
+    int nCars = 0;
+    long long nCarTotal = 0;
+    long long carStride = 0, simStride = 0;
+    int obsDim = 0, stateDim = 0, actDim = 0;
+    cudaStream_t stream = nullptr;
+    int tileSims = 0;
+
+    float* car = nullptr;
+    float* sim = nullptr;
+    float* carOut = nullptr;
+    int* simOut = nullptr;
+    int* diagCar = nullptr;
+    int* diagSim = nullptr;
+    bool diagnostics = false;
+
+    float4* triV = nullptr;
+    float4* triAng = nullptr;
+    int* cellStart = nullptr;
+    int* cellTris = nullptr;
+    int hitWords = 1;
+
+    float *obs = nullptr, *tobs = nullptr, *packed = nullptr, *tpacked = nullptr, *rewards = nullptr;
+    uint8_t *dones = nullptr, *overtime = nullptr, *tovertime = nullptr;
+    int *scoreDiff = nullptr, *episodeTicks = nullptr, *tScoreDiff = nullptr, *tEpisodeTicks = nullptr;
+    void* actions = nullptr;
+    size_t actionCapacity = 0;
+
+    int tick = 0;
+    int maxTicks = REGULATION_TICKS;
+    int overtimeTicks = REGULATION_TICKS;
+    int noTouchTicks = 0;
+
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    float lastTickMs = 0.f;
+    std::string error;
+
+    std::vector<void*> allocations;
+
+    GView view() const
+    {
+        GView g;
+        g.car = GlobSoa{ car, carStride };
+        g.out = GlobSoa{ carOut, carStride };
+        g.sim = GlobSoa{ sim, simStride };
+        g.simOut = simOut;
+        g.nSim = cfg.n_sim;
+        g.nCars = nCars;
+        g.nBlue = cfg.n_blue;
+        g.nOrange = cfg.n_orange;
+        g.seed = cfg.seed;
+        g.simOffset = cfg.sim_offset;
+        return g;
+    }
+    ArenaDev arena() const { return ArenaDev{ triV, triAng, cellStart, cellTris, hitWords }; }
+    Outputs outputs() const
+    {
+        return Outputs{ rewards, dones, scoreDiff, episodeTicks, tScoreDiff, tEpisodeTicks, overtime, tovertime };
+    }
+};
+
+namespace {
+
+carlb_status fail(carlb_env* e, carlb_status s, const std::string& msg)
+{
+    if (e) e->error = msg;
+    else g_createError = msg;
+    return s;
+}
+
+carlb_status cudaFail(carlb_env* e, cudaError_t err, const char* what)
+{
+    return fail(e, CARLB_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(err));
+}
+
+#define ECHECK(e, call)                                            \
+    do {                                                           \
+        cudaError_t err_ = (call);                                 \
+        if (err_ != cudaSuccess) return cudaFail((e), err_, #call); \
+    } while (0)
+
+template <class T>
+cudaError_t allocZero(carlb_env* e, T** p, size_t count)
+{
+    void* v = nullptr;
+    cudaError_t err = cudaMalloc(&v, count * sizeof(T) > 0 ? count * sizeof(T) : 16);
+    if (err != cudaSuccess) return err;
+    e->allocations.push_back(v);
+    *p = static_cast<T*>(v);
+    return cudaMemsetAsync(v, 0, count * sizeof(T), e->stream);
+}
+
+int chooseTileSims(int nCars, int hitWords)
+{
+    if (const char* s = std::getenv("CARLB_TILE_SIMS"))
+    {
+        const int v = std::atoi(s);
+        if (v > 0 && v * nCars <= 256) return v;
+    }
+    int best = 1;
+    for (int ts = 1; ts <= 64 && ts * nCars <= 256; ts++)
+        if (tickSmemBytes(ts, nCars, hitWords, tickThreads(ts, nCars)) <= 112 * 1024) best = ts;
+    return best;
+}
+
+size_t actionRowBytes(carlb_action_kind kind) { return kind == CARLB_ACTIONS_DIRECT ? 32 : 28; }
+
+carlb_status launchTicks(carlb_env* e, carlb_action_kind kind, int nTicks)
+{
+    TickParams p{};
+    p.car = e->car;
+    p.sim = e->sim;
+    p.carOut = e->carOut;
+    p.diagCar = e->diagnostics ? e->diagCar : nullptr;
+    p.diagSim = e->diagnostics ? e->diagSim : nullptr;
+    p.actions = e->actions;
+    p.carStride = e->carStride;
+    p.simStride = e->simStride;
+    p.globalCarBase = e->cfg.sim_offset * e->nCars;
+    p.actionKind = (int)kind;
+    p.nSim = e->cfg.n_sim;
+    p.nCars = e->nCars;
+    p.nBlue = e->cfg.n_blue;
+    p.seed = e->cfg.seed;
+    p.tick0 = e->tick;
+    p.nTicks = nTicks;
+    p.tileSims = e->tileSims;
+    p.compatFlags = e->cfg.compat_flags;
+    ECHECK(e, cudaEventRecord(e->ev0, e->stream));
+    const int err = launchTick(p, e->arena(), e->stream);
+    if (err) return cudaFail(e, (cudaError_t)err, "tick kernel launch");
+    ECHECK(e, cudaEventRecord(e->ev1, e->stream));
+    e->tick += nTicks;
+    return CARLB_OK;
+}
+
+carlb_status stageActions(carlb_env* e, carlb_action_kind kind, const void* src, cudaMemcpyKind dir)
+{
+    if (kind != CARLB_ACTIONS_DISCRETE && kind != CARLB_ACTIONS_CONTINUOUS && kind != CARLB_ACTIONS_DIRECT)
+        return fail(e, CARLB_ERR_VALUE, "unknown action kind");
+    if (!src) return fail(e, CARLB_ERR_VALUE, "actions pointer is null");
+    const size_t bytes = (size_t)e->nCarTotal * actionRowBytes(kind);
+    ECHECK(e, cudaMemcpyAsync(e->actions, src, bytes, dir, e->stream));
+    return CARLB_OK;
+}
+
+// Output packing after a reset / state injection (current outputs only).
+void packCurrent(carlb_env* e, const uint8_t* mask)
+{
+    const GView g = e->view();
+    launchPackObs(g, e->obs, mask, e->obsDim, e->cfg.invert_orange, e->cfg.normalize, e->cfg.previous_controls, e->stream);
+    launchPackState(g, e->packed, e->stateDim, e->tick, 1, mask, e->stream);
+    launchPackRawMatch(g, e->outputs(), mask, e->stream);
+}
+
+carlb_status resetEnv(carlb_env* e)
+{
+    const GView g = e->view();
+    e->tick = 0;
+    launchClear(g, e->stream);
+    launchKickoff(g, 0, e->stream);
+    launchPackObs(g, e->obs, nullptr, e->obsDim, e->cfg.invert_orange, e->cfg.normalize, e->cfg.previous_controls, e->stream);
+    launchPackState(g, e->packed, e->stateDim, e->tick, 1, nullptr, e->stream);
+    launchPackState(g, e->tpacked, e->stateDim, e->tick, 1, nullptr, e->stream);
+    launchPackRewardsDones(g, e->outputs(), e->tick, e->maxTicks, e->overtimeTicks, e->noTouchTicks, e->stream);
+    launchPackRawMatch(g, e->outputs(), nullptr, e->stream);
+    ECHECK(e, cudaGetLastError());
+    return CARLB_OK;
+}
+
+struct FieldMap
+{
+    void* base = nullptr;
+    long long stride = 0;
+    long long rows = 0;
+    int word = 0, width = 0;
+    bool readOnly = false;
+    bool host = false;  // tick counter
+};
+
+bool mapField(carlb_env* e, int field, FieldMap& m)
+{
+    const long long n = e->nCarTotal, ns = e->cfg.n_sim;
+    auto carW = [&](int w, int width) { m.base = e->car; m.stride = e->carStride; m.rows = n; m.word = w; m.width = width; };
+    auto outW = [&](int w, int width) { m.base = e->carOut; m.stride = e->carStride; m.rows = n; m.word = w; m.width = width; };
+    auto simW = [&](int w, int width) { m.base = e->sim; m.stride = e->simStride; m.rows = ns; m.word = w; m.width = width; };
+    switch (field)
+    {
+    case CARLB_F_CAR_POS: carW(C_POS, 3); return true;
+    case CARLB_F_CAR_VEL: carW(C_VEL, 3); return true;
+    case CARLB_F_CAR_ANG: carW(C_ANG, 3); return true;
+    case CARLB_F_CAR_ROT: carW(C_ROT, 4); return true;
+    case CARLB_F_CAR_CEN: carW(C_CEN, 3); return true;
+    case CARLB_F_CAR_IMP: carW(C_IMP, 3); return true;
+    case CARLB_F_CAR_IS_DEMOED: carW(C_DEMOED, 1); return true;
+    case CARLB_F_CAR_DEMO_TIMER: carW(C_DEMO_TIMER, 1); return true;
+    case CARLB_F_CAR_CONTACT_IDX: carW(C_CONTACT_IDX, 1); return true;
+    case CARLB_F_CAR_CONTACT_COOLDOWN: carW(C_CONTACT_CD, 1); return true;
+    case CARLB_F_CAR_BALL_HIT_TICK: carW(C_BALL_HIT_TICK, 1); return true;
+    case CARLB_F_CAR_BALL_CONTACT_TICK: carW(C_BALL_CONTACT_TICK, 1); return true;
+    case CARLB_F_CAR_WHEEL_SOURCE: outW(O_WHEEL_SRC, 4); return true;
+    case CARLB_F_CAR_WHEEL_CONTACT: outW(O_WHEEL_CON, 4); return true;
+    case CARLB_F_CAR_ARENA_CONTACT_TICK: outW(O_ARENA_CONTACT_TICK, 1); return true;
+    case CARLB_F_CAR_CONTROLS: outW(O_CONTROLS, 8); return true;
+    case CARLB_F_CAR_INTERNAL: carW(C_INT, CARLB_INT_WORDS); return true;
+    case CARLB_F_SUSP_SCALARS: carW(C_SUSP, CARLB_SUSP_WORDS); return true;
+    case CARLB_F_SUSP_RAY_DIST: outW(O_RAY_DIST, 4); return true;
+    case CARLB_F_SUSP_RAY_NORMAL: outW(O_RAY_NORMAL, 12); return true;
+    case CARLB_F_SUSP_LAT_FRICTION: carW(C_LAT, 4); return true;
+    case CARLB_F_SUSP_LON_FRICTION: carW(C_LON, 4); return true;
+    case CARLB_F_MAN_COUNT: carW(C_MAN_COUNT, 1); return true;
+    case CARLB_F_MAN_NORMAL0: carW(C_MAN_N0, 3); return true;
+    case CARLB_F_BALL_POS: simW(S_BPOS, 3); return true;
+    case CARLB_F_BALL_VEL: simW(S_BVEL, 3); return true;
+    case CARLB_F_BALL_ANG: simW(S_BANG, 3); return true;
+    case CARLB_F_BALL_IMP: simW(S_BIMP, 3); return true;
+    case CARLB_F_BALL_INT_POS: simW(S_IPOS, 3); return true;
+    case CARLB_F_BALL_INT_VEL: simW(S_IVEL, 3); return true;
+    case CARLB_F_BALL_EXP_POS: simW(S_EPOS, 3); return true;
+    case CARLB_F_BALL_EXP_VEL: simW(S_EVEL, 3); return true;
+    case CARLB_F_BALL_INT_VALID: simW(S_IVALID, 1); return true;
+    case CARLB_F_EPISODE_TICKS: simW(S_EP_TICKS, 1); return true;
+    case CARLB_F_LAST_TOUCH_TICKS: simW(S_LAST_TOUCH, 1); return true;
+    case CARLB_F_BALL_ARENA_CONTACT_TICK:
+        m.base = e->simOut; m.stride = e->simStride; m.rows = ns; m.word = 0; m.width = 1; return true;
+    case CARLB_F_GOALS: simW(S_GOALS, 5); return true;
+    case CARLB_F_PAD_COOLDOWNS: simW(S_PADS, NUM_BOOST_PADS); return true;
+    case CARLB_F_TICK_COUNT: m.rows = 1; m.width = 1; m.host = true; return true;
+    case CARLB_F_DIAG_CELL_IDX:
+        m.base = e->diagCar; m.stride = e->carStride; m.rows = n; m.word = 0; m.width = 1; m.readOnly = true; return true;
+    case CARLB_F_DIAG_NUM_TRIS:
+        m.base = e->diagCar; m.stride = e->carStride; m.rows = n; m.word = 1; m.width = 1; m.readOnly = true; return true;
+    case CARLB_F_DIAG_SAT_PAIRS:
+        m.base = e->diagCar; m.stride = e->carStride; m.rows = n; m.word = 2; m.width = 1 + MAX_CAR_TRI_PAIRS;
+        m.readOnly = true; return true;
+    case CARLB_F_DIAG_CC_COUNT:
+    {
+        const int pairs = e->nCars * (e->nCars - 1) / 2;
+        m.base = e->diagSim; m.stride = e->simStride; m.rows = ns; m.word = 0; m.width = pairs > 0 ? pairs : 1;
+        m.readOnly = true; return true;
+    }
+    default:
+        return false;
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+carlb_status carlb_destroy(carlb_env* e);
+
+static carlb_status initEnv(carlb_env* p, const carlb_config* cfg)
+{
+    std::string err;
+    const auto host = hostArena(arenaObjPath(libraryDir() + "/_data/arena.obj"), err);
+    if (!host) return fail(p, CARLB_ERR_STATE, err);
+
+    p->cfg = *cfg;
+    p->nCars = cfg->n_blue + cfg->n_orange;
+    p->nCarTotal = (long long)cfg->n_sim * p->nCars;
+    p->obsDim = observationDim(p->nCars, cfg->previous_controls != 0);
+    p->stateDim = packedStateDim(p->nCars);
+    p->actDim = p->nCars * ACT_PER_CAR;
+    p->hitWords = (host->maxCellTris + 31) / 32;
+    p->tileSims = chooseTileSims(p->nCars, p->hitWords);
+    // Pad to whole tiles (rounded to 4 rows) so every per-word row is 16-byte aligned.
+    const long long simPad = ((long long)cfg->n_sim + p->tileSims - 1) / p->tileSims * p->tileSims;
+    p->simStride = (simPad + 3) / 4 * 4;
+    p->carStride = (simPad * p->nCars + 3) / 4 * 4;
+
+    ECHECK(p, cudaSetDevice(cfg->device));
+    ECHECK(p, cudaStreamCreateWithFlags(&p->stream, cudaStreamNonBlocking));
+    ECHECK(p, cudaEventCreate(&p->ev0));
+    ECHECK(p, cudaEventCreate(&p->ev1));
+
+    ECHECK(p, allocZero(p, &p->car, (size_t)NCW * p->carStride));
+    ECHECK(p, allocZero(p, &p->sim, (size_t)NSW * p->simStride));
+    ECHECK(p, allocZero(p, &p->carOut, (size_t)NOW * p->carStride));
+    ECHECK(p, allocZero(p, &p->simOut, (size_t)NSOW * p->simStride));
+    ECHECK(p, allocZero(p, &p->obs, (size_t)p->nCarTotal * p->obsDim));
+    ECHECK(p, allocZero(p, &p->tobs, (size_t)p->nCarTotal * p->obsDim));
+    ECHECK(p, allocZero(p, &p->packed, (size_t)cfg->n_sim * p->stateDim));
+    ECHECK(p, allocZero(p, &p->tpacked, (size_t)cfg->n_sim * p->stateDim));
+    ECHECK(p, allocZero(p, &p->rewards, (size_t)cfg->n_sim));
+    ECHECK(p, allocZero(p, &p->dones, (size_t)cfg->n_sim));
+    ECHECK(p, allocZero(p, &p->overtime, (size_t)cfg->n_sim));
+    ECHECK(p, allocZero(p, &p->tovertime, (size_t)cfg->n_sim));
+    ECHECK(p, allocZero(p, &p->scoreDiff, (size_t)cfg->n_sim));
+    ECHECK(p, allocZero(p, &p->episodeTicks, (size_t)cfg->n_sim));
+    ECHECK(p, allocZero(p, &p->tScoreDiff, (size_t)cfg->n_sim));
+    ECHECK(p, allocZero(p, &p->tEpisodeTicks, (size_t)cfg->n_sim));
+    p->actionCapacity = (size_t)p->nCarTotal * 32;
+    {
+        uint8_t* a = nullptr;
+        ECHECK(p, allocZero(p, &a, p->actionCapacity));
+        p->actions = a;
+    }
+
+    // Arena tables: vertices expanded per triangle (flags in vertex 0's w).
+    const int nTris = host->nTris();
+    std::vector<float4> triV((size_t)nTris * 3), triAng(nTris);
+    for (int t = 0; t < nTris; t++)
+    {
+        for (int k = 0; k < 3; k++)
+        {
+            const int v = host->tris[3 * t + k];
+            float w = 0.f;
+            if (k == 0) std::memcpy(&w, &host->triFlags[t], 4);
+            triV[3 * t + k] = make_float4(host->verts[3 * v], host->verts[3 * v + 1], host->verts[3 * v + 2], w);
+        }
+        triAng[t] = make_float4(host->edgeAngles[3 * t], host->edgeAngles[3 * t + 1], host->edgeAngles[3 * t + 2], 0.f);
+    }
+    ECHECK(p, allocZero(p, &p->triV, triV.size()));
+    ECHECK(p, allocZero(p, &p->triAng, triAng.size()));
+    ECHECK(p, allocZero(p, &p->cellStart, host->cellStart.size()));
+    ECHECK(p, allocZero(p, &p->cellTris, host->cellTris.size()));
+    ECHECK(p, cudaMemcpyAsync(p->triV, triV.data(), triV.size() * sizeof(float4), cudaMemcpyHostToDevice, p->stream));
+    ECHECK(p, cudaMemcpyAsync(p->triAng, triAng.data(), triAng.size() * sizeof(float4), cudaMemcpyHostToDevice, p->stream));
+    ECHECK(p, cudaMemcpyAsync(p->cellStart, host->cellStart.data(), host->cellStart.size() * 4, cudaMemcpyHostToDevice, p->stream));
+    ECHECK(p, cudaMemcpyAsync(p->cellTris, host->cellTris.data(), host->cellTris.size() * 4, cudaMemcpyHostToDevice, p->stream));
+
+    Tables tables;
+    buildTables(tables);
+    ECHECK(p, (cudaError_t)uploadTickTables(tables));
+    ECHECK(p, (cudaError_t)uploadEnvioTables(tables));
+
+    const carlb_status st = resetEnv(p);
+    if (st != CARLB_OK) return st;
+    ECHECK(p, cudaStreamSynchronize(p->stream));
+    return CARLB_OK;
+}
+
+carlb_status carlb_create(const carlb_config* cfg, carlb_env** out)
+{
+    if (!out) return fail(nullptr, CARLB_ERR_VALUE, "out is null");
+    *out = nullptr;
+    if (!cfg) return fail(nullptr, CARLB_ERR_VALUE, "config is null");
+    if (cfg->n_sim < 1) return fail(nullptr, CARLB_ERR_VALUE, "n_sim must be at least 1");
+    if (cfg->n_blue < 0 || cfg->n_orange < 0 || cfg->n_blue + cfg->n_orange < 1)
+        return fail(nullptr, CARLB_ERR_VALUE, "team sizes must be non-negative with at least one car");
+    if (cfg->n_blue > 4 || cfg->n_orange > 4)
+        return fail(nullptr, CARLB_ERR_VALUE, "at most 4 cars per team (4 kickoff spots per team)");
+    if (cfg->frameskip < 1) return fail(nullptr, CARLB_ERR_VALUE, "frameskip must be at least 1");
+    if (cfg->sim_offset < 0) return fail(nullptr, CARLB_ERR_VALUE, "sim_offset must be non-negative");
+
+    carlb_env* p = new carlb_env;
+    const carlb_status st = initEnv(p, cfg);
+    if (st != CARLB_OK)
+    {
+        g_createError = p->error;
+        carlb_destroy(p);
+        return st;
+    }
+    *out = p;
+    return CARLB_OK;
+}
+
+carlb_status carlb_destroy(carlb_env* e)
+{
+    if (!e) return CARLB_OK;
+    cudaSetDevice(e->cfg.device);
+    if (e->stream) cudaStreamSynchronize(e->stream);
+    for (void* v : e->allocations) cudaFree(v);
+    if (e->ev0) cudaEventDestroy(e->ev0);
+    if (e->ev1) cudaEventDestroy(e->ev1);
+    if (e->stream) cudaStreamDestroy(e->stream);
+    delete e;
+    return CARLB_OK;
+}
+
+const char* carlb_last_error(const carlb_env* e) { return e ? e->error.c_str() : g_createError.c_str(); }
+
+carlb_status carlb_ticks(carlb_env* e, carlb_action_kind kind, const void* actions, int32_t n)
+{
+    if (!e) return fail(nullptr, CARLB_ERR_VALUE, "env is null");
+    if (n < 0) return fail(e, CARLB_ERR_VALUE, "n_ticks must be non-negative");
+    carlb_status s = stageActions(e, kind, actions, cudaMemcpyDeviceToDevice);
+    if (s != CARLB_OK) return s;
+    return launchTicks(e, kind, n);
+}
+
+carlb_status carlb_ticks_host(carlb_env* e, carlb_action_kind kind, const void* hostActions, int32_t n,
+                              float* hostRewards)
+{
+    if (!e) return fail(nullptr, CARLB_ERR_VALUE, "env is null");
+    if (n < 0) return fail(e, CARLB_ERR_VALUE, "n_ticks must be non-negative");
+    carlb_status s = stageActions(e, kind, hostActions, cudaMemcpyHostToDevice);
+    if (s != CARLB_OK) return s;
+    s = launchTicks(e, kind, n);
+    if (s != CARLB_OK) return s;
+    if (hostRewards)
+    {
+        launchPackRewardsDones(e->view(), e->outputs(), e->tick, e->maxTicks, e->overtimeTicks, e->noTouchTicks, e->stream);
+        ECHECK(e, cudaMemcpyAsync(hostRewards, e->rewards, (size_t)e->cfg.n_sim * 4, cudaMemcpyDeviceToHost, e->stream));
+    }
+    ECHECK(e, cudaStreamSynchronize(e->stream));
+    return CARLB_OK;
+}
+
+carlb_status carlb_env_step(carlb_env* e, carlb_action_kind kind, const void* actions)
+{
+    if (!e) return fail(nullptr, CARLB_ERR_VALUE, "env is null");
+    if (kind == CARLB_ACTIONS_DIRECT) return fail(e, CARLB_ERR_VALUE, "env_step takes discrete or continuous actions");
+    carlb_status s = stageActions(e, kind, actions, cudaMemcpyDeviceToDevice);
+    if (s != CARLB_OK) return s;
+    s = launchTicks(e, kind, e->cfg.frameskip);
+    if (s != CARLB_OK) return s;
+    const GView g = e->view();
+    const Outputs o = e->outputs();
+    launchPackRewardsDones(g, o, e->tick, e->maxTicks, e->overtimeTicks, e->noTouchTicks, e->stream);
+    launchPackState(g, e->tpacked, e->stateDim, e->tick, e->cfg.frameskip, nullptr, e->stream);
+    launchPackObs(g, e->tobs, e->dones, e->obsDim, e->cfg.invert_orange, e->cfg.normalize, e->cfg.previous_controls, e->stream);
+    launchResetDones(g, e->tick, e->maxTicks, e->overtimeTicks, e->noTouchTicks, e->stream);
+    launchPackRawMatch(g, o, nullptr, e->stream);
+    launchPackObs(g, e->obs, nullptr, e->obsDim, e->cfg.invert_orange, e->cfg.normalize, e->cfg.previous_controls, e->stream);
+    launchPackState(g, e->packed, e->stateDim, e->tick, 1, nullptr, e->stream);
+    ECHECK(e, cudaGetLastError());
+    return CARLB_OK;
+}
+
+carlb_status carlb_reset(carlb_env* e)
+{
+    if (!e) return fail(nullptr, CARLB_ERR_VALUE, "env is null");
+    return resetEnv(e);
+}
+
+carlb_status carlb_reset_dones(carlb_env* e)
+{
+    if (!e) return fail(nullptr, CARLB_ERR_VALUE, "env is null");
+    launchResetDones(e->view(), e->tick, e->maxTicks, e->overtimeTicks, e->noTouchTicks, e->stream);
+    ECHECK(e, cudaGetLastError());
+    return CARLB_OK;
+}
+
+carlb_status carlb_apply_reset_state(carlb_env* e, int32_t n, const float* ballPos, const float* ballVel,
+                                     const float* ballAng, const float* carPos, const float* carRot,
+                                     const float* carVel, const float* carAng, const void* demoed, int32_t demoedIsByte,
+                                     const float* boost, const float* internal, const int32_t* blue,
+                                     const int32_t* orange, const int32_t* ticks, const int64_t* indices,
+                                     const uint8_t* mask)
+{
+    if (!e) return fail(nullptr, CARLB_ERR_VALUE, "env is null");
+    if (mask && indices) return fail(e, CARLB_ERR_VALUE, "specify reset_mask or simulation_indices, not both");
+    if (mask) n = e->cfg.n_sim;
+    if (n < 0 || n > e->cfg.n_sim) return fail(e, CARLB_ERR_VALUE, "too many simulation_indices");
+    if (!ballPos || !ballVel || !ballAng || !carPos || !carRot || !carVel || !carAng || !demoed)
+        return fail(e, CARLB_ERR_VALUE, "ball and car inputs are required");
+    if ((blue == nullptr) != (orange == nullptr) || (blue == nullptr) != (ticks == nullptr))
+        return fail(e, CARLB_ERR_VALUE, "blue_score, orange_score and episode_ticks must be supplied together");
+    if (n == 0) return CARLB_OK;
+    const GView g = e->view();
+    launchResetPads(g, n, indices, mask, e->stream);
+    launchSetBall(g, BallInputs{ ballPos, ballVel, ballAng }, n, indices, mask, e->stream);
+    launchSetCar(g, e->arena(), CarInputs{ carPos, carRot, carVel, carAng, demoed, demoedIsByte, boost, internal }, n,
+                 indices, mask, e->stream);
+    if (blue) launchSetMatch(g, blue, orange, ticks, n, indices, mask, e->stream);
+    packCurrent(e, mask);
+    ECHECK(e, cudaGetLastError());
+    return CARLB_OK;
+}
+
+carlb_status carlb_set_ball(carlb_env* e, int32_t n, const float* pos, const float* vel, const float* ang,
+                            const int64_t* indices)
+{
+    if (!e) return fail(nullptr, CARLB_ERR_VALUE, "env is null");
+    if (n < 0 || n > e->cfg.n_sim) return fail(e, CARLB_ERR_VALUE, "too many simulation_indices");
+    if (!pos || !vel || !ang) return fail(e, CARLB_ERR_VALUE, "ball inputs are required");
+    const GView g = e->view();
+    launchSetBall(g, BallInputs{ pos, vel, ang }, n, indices, nullptr, e->stream);
+    launchPackObs(g, e->obs, nullptr, e->obsDim, e->cfg.invert_orange, e->cfg.normalize, e->cfg.previous_controls, e->stream);
+    launchPackState(g, e->packed, e->stateDim, e->tick, 1, nullptr, e->stream);
+    launchPackState(g, e->tpacked, e->stateDim, e->tick, 1, nullptr, e->stream);
+    ECHECK(e, cudaGetLastError());
+    ECHECK(e, cudaStreamSynchronize(e->stream));
+    return CARLB_OK;
+}
+
+carlb_status carlb_set_car(carlb_env* e, int32_t n, const float* pos, const float* rot, const float* vel,
+                           const float* ang, const void* demoed, int32_t demoedIsByte, const float* boost,
+                           const float* internal, const int64_t* indices)
+{
+    if (!e) return fail(nullptr, CARLB_ERR_VALUE, "env is null");
+    if (n < 0 || n > e->cfg.n_sim) return fail(e, CARLB_ERR_VALUE, "too many simulation_indices");
+    if (!pos || !rot || !vel || !ang || !demoed) return fail(e, CARLB_ERR_VALUE, "car inputs are required");
+    const GView g = e->view();
+    launchSetCar(g, e->arena(), CarInputs{ pos, rot, vel, ang, demoed, demoedIsByte, boost, internal }, n, indices,
+                 nullptr, e->stream);
+    launchPackObs(g, e->obs, nullptr, e->obsDim, e->cfg.invert_orange, e->cfg.normalize, e->cfg.previous_controls, e->stream);
+    launchPackState(g, e->packed, e->stateDim, e->tick, 1, nullptr, e->stream);
+    launchPackState(g, e->tpacked, e->stateDim, e->tick, 1, nullptr, e->stream);
+    ECHECK(e, cudaGetLastError());
+    ECHECK(e, cudaStreamSynchronize(e->stream));
+    return CARLB_OK;
+}
+
+carlb_status carlb_set_match_state(carlb_env* e, int32_t n, const int32_t* blue, const int32_t* orange,
+                                   const int32_t* ticks, const int64_t* indices)
+{
+    if (!e) return fail(nullptr, CARLB_ERR_VALUE, "env is null");
+    if (n < 0 || n > e->cfg.n_sim) return fail(e, CARLB_ERR_VALUE, "too many simulation_indices");
+    if (!blue || !orange || !ticks) return fail(e, CARLB_ERR_VALUE, "score and tick inputs are required");
+    launchSetMatch(e->view(), blue, orange, ticks, n, indices, nullptr, e->stream);
+    ECHECK(e, cudaGetLastError());
+    return CARLB_OK;
+}
+
+carlb_status carlb_reset_boost_pads(carlb_env* e, int32_t n, const int64_t* indices)
+{
+    if (!e) return fail(nullptr, CARLB_ERR_VALUE, "env is null");
+    if (n < 0 || n > e->cfg.n_sim) return fail(e, CARLB_ERR_VALUE, "too many simulation_indices");
+    launchResetPads(e->view(), n, indices, nullptr, e->stream);
+    ECHECK(e, cudaGetLastError());
+    ECHECK(e, cudaStreamSynchronize(e->stream));
+    return CARLB_OK;
+}
+
+carlb_status carlb_get_buffer(carlb_env* e, carlb_buffer which, void** data, int64_t shape[3], int32_t* ndim,
+                              carlb_dtype* dtype)
+{
+    if (!e || !data || !shape || !ndim || !dtype) return fail(e, CARLB_ERR_VALUE, "null argument");
+    const int64_t ns = e->cfg.n_sim;
+    shape[0] = ns;
+    shape[1] = shape[2] = 0;
+    *ndim = 1;
+    switch (which)
+    {
+    case CARLB_BUF_OBS:
+    case CARLB_BUF_TRANSITION_OBS:
+        *data = which == CARLB_BUF_OBS ? e->obs : e->tobs;
+        shape[1] = e->nCars; shape[2] = e->obsDim; *ndim = 3; *dtype = CARLB_F32; return CARLB_OK;
+    case CARLB_BUF_STATE:
+    case CARLB_BUF_TRANSITION_STATE:
+        *data = which == CARLB_BUF_STATE ? e->packed : e->tpacked;
+        shape[1] = e->stateDim; *ndim = 2; *dtype = CARLB_F32; return CARLB_OK;
+    case CARLB_BUF_REWARDS: *data = e->rewards; *dtype = CARLB_F32; return CARLB_OK;
+    case CARLB_BUF_DONES: *data = e->dones; *dtype = CARLB_BOOL; return CARLB_OK;
+    case CARLB_BUF_SCORE_DIFFERENCE: *data = e->scoreDiff; *dtype = CARLB_I32; return CARLB_OK;
+    case CARLB_BUF_EPISODE_TICKS: *data = e->episodeTicks; *dtype = CARLB_I32; return CARLB_OK;
+    case CARLB_BUF_TRANSITION_SCORE_DIFFERENCE: *data = e->tScoreDiff; *dtype = CARLB_I32; return CARLB_OK;
+    case CARLB_BUF_TRANSITION_EPISODE_TICKS: *data = e->tEpisodeTicks; *dtype = CARLB_I32; return CARLB_OK;
+    case CARLB_BUF_OVERTIME: *data = e->overtime; *dtype = CARLB_BOOL; return CARLB_OK;
+    case CARLB_BUF_TRANSITION_OVERTIME: *data = e->tovertime; *dtype = CARLB_BOOL; return CARLB_OK;
+    default: return fail(e, CARLB_ERR_VALUE, "unknown buffer");
+    }
+}
+
+carlb_status carlb_set_limit(carlb_env* e, carlb_limit which, int32_t v)
+{
+    if (!e) return fail(nullptr, CARLB_ERR_VALUE, "env is null");
+    switch (which)
+    {
+    case CARLB_LIMIT_MAX_TICKS:
+        if (v < 1) return fail(e, CARLB_ERR_VALUE, "max_ticks must be at least 1");
+        e->maxTicks = v; return CARLB_OK;
+    case CARLB_LIMIT_OVERTIME_TIMEOUT_TICKS:
+        if (v < 1) return fail(e, CARLB_ERR_VALUE, "overtime_timeout_ticks must be at least 1");
+        e->overtimeTicks = v; return CARLB_OK;
+    case CARLB_LIMIT_NO_TOUCH_TIMEOUT_TICKS:
+        if (v < 0) return fail(e, CARLB_ERR_VALUE, "no_touch_timeout_ticks must be non-negative");
+        e->noTouchTicks = v; return CARLB_OK;
+    case CARLB_LIMIT_FRAMESKIP:
+        if (v < 1) return fail(e, CARLB_ERR_VALUE, "frameskip must be at least 1");
+        e->cfg.frameskip = v; return CARLB_OK;
+    default: return fail(e, CARLB_ERR_VALUE, "unknown limit");
+    }
+}
+
+carlb_status carlb_get_limit(const carlb_env* e, carlb_limit which, int32_t* v)
+{
+    if (!e || !v) return CARLB_ERR_VALUE;
+    switch (which)
+    {
+    case CARLB_LIMIT_MAX_TICKS: *v = e->maxTicks; return CARLB_OK;
+    case CARLB_LIMIT_OVERTIME_TIMEOUT_TICKS: *v = e->overtimeTicks; return CARLB_OK;
+    case CARLB_LIMIT_NO_TOUCH_TIMEOUT_TICKS: *v = e->noTouchTicks; return CARLB_OK;
+    case CARLB_LIMIT_FRAMESKIP: *v = e->cfg.frameskip; return CARLB_OK;
+    default: return CARLB_ERR_VALUE;
+    }
+}
+
+carlb_status carlb_dims(const carlb_env* e, int32_t dims[5])
+{
+    if (!e || !dims) return CARLB_ERR_VALUE;
+    dims[0] = e->cfg.n_sim;
+    dims[1] = e->nCars;
+    dims[2] = e->obsDim;
+    dims[3] = e->actDim;
+    dims[4] = e->stateDim;
+    return CARLB_OK;
+}
+
+void* carlb_stream(const carlb_env* e) { return e ? (void*)e->stream : nullptr; }
+
+carlb_status carlb_synchronize(carlb_env* e)
+{
+    if (!e) return fail(nullptr, CARLB_ERR_VALUE, "env is null");
+    ECHECK(e, cudaStreamSynchronize(e->stream));
+    return CARLB_OK;
+}
+
+carlb_status carlb_field_shape(const carlb_env* e, carlb_field field, int64_t* rows, int32_t* width)
+{
+    if (!e || !rows || !width) return CARLB_ERR_VALUE;
+    FieldMap m;
+    if (!mapField(const_cast<carlb_env*>(e), field, m)) return CARLB_ERR_VALUE;
+    *rows = m.rows;
+    *width = m.width;
+    return CARLB_OK;
+}
+
+carlb_status carlb_read_field(carlb_env* e, carlb_field field, void* out)
+{
+    if (!e || !out) return fail(e, CARLB_ERR_VALUE, "null argument");
+    FieldMap m;
+    if (!mapField(e, field, m)) return fail(e, CARLB_ERR_VALUE, "unknown field");
+    ECHECK(e, cudaStreamSynchronize(e->stream));
+    uint32_t* dst = static_cast<uint32_t*>(out);
+    if (m.host)
+    {
+        dst[0] = (uint32_t)e->tick;
+        return CARLB_OK;
+    }
+    std::vector<uint32_t> col((size_t)m.rows);
+    for (int k = 0; k < m.width; k++)
+    {
+        const uint32_t* src = static_cast<const uint32_t*>(m.base) + (long long)(m.word + k) * m.stride;
+        ECHECK(e, cudaMemcpy(col.data(), src, (size_t)m.rows * 4, cudaMemcpyDeviceToHost));
+        for (long long r = 0; r < m.rows; r++) dst[r * m.width + k] = col[r];
+    }
+    return CARLB_OK;
+}
+
+carlb_status carlb_write_field(carlb_env* e, carlb_field field, const void* in)
+{
+    if (!e || !in) return fail(e, CARLB_ERR_VALUE, "null argument");
+    FieldMap m;
+    if (!mapField(e, field, m)) return fail(e, CARLB_ERR_VALUE, "unknown field");
+    if (m.readOnly) return fail(e, CARLB_ERR_VALUE, "field is read-only");
+    ECHECK(e, cudaStreamSynchronize(e->stream));
+    const uint32_t* src = static_cast<const uint32_t*>(in);
+    if (m.host)
+    {
+        e->tick = (int)src[0];
+        return CARLB_OK;
+    }
+    std::vector<uint32_t> col((size_t)m.rows);
+    for (int k = 0; k < m.width; k++)
+    {
+        for (long long r = 0; r < m.rows; r++) col[r] = src[r * m.width + k];
+        uint32_t* dst = static_cast<uint32_t*>(m.base) + (long long)(m.word + k) * m.stride;
+        ECHECK(e, cudaMemcpy(dst, col.data(), (size_t)m.rows * 4, cudaMemcpyHostToDevice));
+    }
+    return CARLB_OK;
+}
+
+carlb_status carlb_last_tick_ms(const carlb_env* e, float* ms)
+{
+    if (!e || !ms) return CARLB_ERR_VALUE;
+    const cudaError_t err = cudaEventElapsedTime(ms, e->ev0, e->ev1);
+    return err == cudaSuccess ? CARLB_OK : CARLB_ERR_CUDA;
+}
+
+carlb_status carlb_set_diagnostics(carlb_env* e, int32_t enabled)
+{
+    if (!e) return fail(nullptr, CARLB_ERR_VALUE, "env is null");
+    if (enabled && !e->diagCar)
+    {
+        ECHECK(e, allocZero(e, &e->diagCar, (size_t)DIAG_CAR_WORDS * e->carStride));
+        ECHECK(e, allocZero(e, &e->diagSim, (size_t)DIAG_SIM_WORDS * e->simStride));
+    }
+    e->diagnostics = enabled != 0;
+    return CARLB_OK;
+}
+
+}  // extern "C"

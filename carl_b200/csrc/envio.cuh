@@ -1,0 +1,67 @@
+// Launch wrappers for reset, state injection and output packing (envio.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "cb_state.cuh"
+#include "cb_tables.hpp"
+#include "tick.cuh"
+
+namespace cb {
+
+// Global-memory view of one env's state.
+struct GView
+{
+    GlobSoa car;         // NCW words per car
+    GlobSoa out;         // NOW words per car
+    GlobSoa sim;         // NSW words per sim
+    int* simOut;         // [nSim] ball-arena contact tick (written by resets only)
+    int nSim, nCars, nBlue, nOrange, seed;
+    long long simOffset; // env-global index of sim 0
+};
+
+struct Outputs
+{
+    float* rewards;
+    uint8_t* dones;
+    int* scoreDiff;
+    int* episodeTicks;
+    int* transitionScoreDiff;
+    int* transitionEpisodeTicks;
+    uint8_t* overtime;
+    uint8_t* transitionOvertime;
+};
+
+struct BallInputs
+{
+    const float *pos, *vel, *ang;  // [n, 3]
+};
+
+struct CarInputs
+{
+    const float *pos, *rot, *vel, *ang;  // [n, nCars, 3|4]
+    const void* demoed;                  // [n, nCars] u8 or i32
+    int demoedIsByte;
+    const float* boost;                  // [n, nCars] or null
+    const float* internal;               // [n, nCars, CAR_INTERNAL_SIZE] or null
+};
+
+int uploadEnvioTables(const Tables& t);
+void launchClear(const GView& g, cudaStream_t s);
+void launchKickoff(const GView& g, int tick, cudaStream_t s);
+void launchResetDones(const GView& g, int tick, int maxTicks, int overtimeTicks, int noTouchTicks, cudaStream_t s);
+void launchPackObs(const GView& g, float* out, const uint8_t* mask, int obsDim, bool invertOrange, bool normalize,
+                   bool previousControls, cudaStream_t s);
+void launchPackState(const GView& g, float* out, int stateDim, int tick, int touchWindow, const uint8_t* mask,
+                     cudaStream_t s);
+void launchPackRewardsDones(const GView& g, const Outputs& o, int tick, int maxTicks, int overtimeTicks,
+                            int noTouchTicks, cudaStream_t s);
+void launchPackRawMatch(const GView& g, const Outputs& o, const uint8_t* mask, cudaStream_t s);
+void launchSetBall(const GView& g, const BallInputs& in, int n, const int64_t* idx, const uint8_t* mask, cudaStream_t s);
+void launchSetCar(const GView& g, const ArenaDev& a, const CarInputs& in, int n, const int64_t* idx,
+                  const uint8_t* mask, cudaStream_t s);
+void launchSetMatch(const GView& g, const int32_t* blue, const int32_t* orange, const int32_t* ticks, int n,
+                    const int64_t* idx, const uint8_t* mask, cudaStream_t s);
+void launchResetPads(const GView& g, int n, const int64_t* idx, const uint8_t* mask, cudaStream_t s);
+
+}  // namespace cb

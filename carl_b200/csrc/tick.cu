@@ -1,0 +1,840 @@
+// Fused tick kernel.
+//
+// One CTA owns a tile of `tileSims` consecutive sims.  It copies the tile's
+// persistent state (76 words per car, 66 per sim) from HBM into shared memory
+// once, runs `nTicks` complete ticks on it, and copies it back once: between
+// ticks nothing leaves the SM.  Within a tick the stages run in the
+// reference's order (jwmccarthy/CARL src/RLEnvironment.cu:166-211):
+//
+//   begin step -> broadphase -> suspension raycast -> controls -> SAT/clip ->
+//   suspension + manifold + solve -> car-car -> ball (arena, cars, integrate,
+//   goal) -> integrate cars -> finish tick (impulses, demo respawn) -> pads
+//
+// and are mapped onto the CTA as
+//   * per-car stages: one thread per car;
+//   * the (car, candidate triangle) work of raycast and SAT: flattened over the
+//     whole tile with a block scan and spread evenly over all threads (cells hold
+//     0-262 triangles, so per-car loops would leave most lanes idle); the wheel
+//     ray minimum is an atomicMin on (distance bits, candidate) keys, which picks
+//     the same triangle as the reference's first-minimum scan; SAT hits are a
+//     per-car bitmask of candidate numbers, processed in candidate order;
+//   * per-sim stages (car-car pairs, ball): one warp per sim; pair gates, ball
+//     triangle tests and ball-car gates run across lanes, the order-dependent
+//     solves on lane 0.
+// All physics arithmetic lives in cb_*.cuh and keeps the reference's fp32
+// operation order (the file is compiled with --fmad=false).
+#include "tick.cuh"
+
+#include <cuda_runtime.h>
+
+#include "cb_misc.cuh"
+
+namespace cb {
+
+namespace {
+
+constexpr int WARP_HIT_BUF = 256;    // ball-arena triangle hits gathered per warp
+constexpr int WARP_WORDS = WARP_HIT_BUF + 8;
+constexpr unsigned FULL = 0xffffffffu;
+
+struct Layout
+{
+    int TC, TS, W, HW;
+    int cw, sw, cell, cnt, pre, rs, hits, wsum, key, warp, total;
+};
+
+CB_HD Layout layoutOf(int tileSims, int nCars, int hitWords, int threads)
+{
+    Layout L;
+    L.TS = tileSims;
+    L.TC = tileSims * nCars;
+    L.W = threads / 32;
+    L.HW = hitWords;
+    int o = 0;
+    L.cw = o;   o += NCW * L.TC;
+    L.sw = o;   o += NSW * L.TS;
+    L.cell = o; o += L.TC;
+    L.cnt = o;  o += L.TC;
+    L.pre = o;  o += L.TC + 1;
+    L.rs = o;   o += 15 * L.TC;
+    L.hits = o; o += L.HW * L.TC;
+    L.wsum = o; o += 32;
+    o = (o + 1) & ~1;  // 8-byte alignment for the 64-bit keys
+    L.key = o;  o += 8 * L.TC;
+    L.warp = o; o += L.W * WARP_WORDS;
+    L.total = o;
+    return L;
+}
+
+__device__ __forceinline__ float rayLen(int w) { return suspRayLength(w); }
+
+__device__ __forceinline__ void loadTri(const ArenaDev& a, int tri, V3& v0, V3& v1, V3& v2, int& flags)
+{
+    const float4 p0 = __ldg(&a.triV[3 * tri]);
+    const float4 p1 = __ldg(&a.triV[3 * tri + 1]);
+    const float4 p2 = __ldg(&a.triV[3 * tri + 2]);
+    v0 = V3{ p0.x, p0.y, p0.z };
+    v1 = V3{ p1.x, p1.y, p1.z };
+    v2 = V3{ p2.x, p2.y, p2.z };
+    flags = __float_as_int(p0.w);
+}
+
+__device__ __forceinline__ V3 triAngles(const ArenaDev& a, int tri)
+{
+    const float4 g = __ldg(&a.triAng[tri]);
+    return V3{ g.x, g.y, g.z };
+}
+
+__device__ __forceinline__ unsigned long long rayKey(float dist, unsigned cand)
+{
+    return ((unsigned long long)__float_as_uint(dist) << 32) | cand;
+}
+
+// Decodes the controls of car `gi` (env-global row in the action array).
+__device__ Controls decodeAction(const void* actions, int kind, long long row)
+{
+    if (kind == ACT_DISCRETE)
+    {
+        const int32_t* a = static_cast<const int32_t*>(actions) + row * 7;
+        int32_t v[7];
+        #pragma unroll
+        for (int k = 0; k < 7; k++) v[k] = a[k];
+        return decodeDiscrete(v);
+    }
+    if (kind == ACT_CONTINUOUS)
+    {
+        const float* a = static_cast<const float*>(actions) + row * 7;
+        float v[7];
+        #pragma unroll
+        for (int k = 0; k < 7; k++) v[k] = a[k];
+        return decodeContinuous(v);
+    }
+    const float* a = static_cast<const float*>(actions) + row * 8;
+    Controls c;
+    c.throttle = a[0];
+    c.steer = a[1];
+    c.yaw = a[2];
+    c.pitch = a[3];
+    c.roll = a[4];
+    c.jump = __float_as_int(a[5]);
+    c.boost = __float_as_int(a[6]);
+    c.slide = __float_as_int(a[7]);
+    return c;
+}
+
+// ---- ball stage of one sim, executed by one warp ---------------------------------------
+
+__device__ void ballStage(const SmemSoa& cars, const SmemSoa& sims, int s, int nCars, int tick,
+                          const ArenaDev& arena, int* wbuf, int lane)
+{
+    const int carBase = s * nCars;
+    const V3 ballVel = sims.v(S_BVEL, s);
+    const V3 ballAng = sims.v(S_BANG, s);
+    const bool sleeping = lensq(ballVel) == 0.f && lensq(ballAng) == 0.f;
+    const V3 exportedPos = sims.v(S_BPOS, s);
+    const bool valid = sims.n(S_IVALID, s) != 0;
+
+    V3 posBT = valid && lensq(exportedPos - sims.v(S_EPOS, s)) == 0.f ? sims.v(S_IPOS, s) : exportedPos * .02f;
+    V3 velBT = valid && lensq(ballVel - sims.v(S_EVEL, s)) == 0.f ? sims.v(S_IVEL, s) : ballVel * .02f;
+    const V3 dampedBT = sleeping ? velBT : velBT * powf(1.f - BALL_DRAG, PHYS_DT);
+    const V3 preSolveBT = sleeping ? velBT : dampedBT + (V3{ 0.f, 0.f, GRAVITY_Z } * .02f) * PHYS_DT;
+    const V3 velNoExt = dampedBT * 50.f;
+    const V3 preSolveVel = preSolveBT * 50.f;
+    V3 pushVel = v3zero();
+
+    if (!sleeping)
+    {
+        // Arena triangles of the grid cells around the ball, tested across lanes.
+        const V3 center = exportedPos;
+        const V3 ext = v3fill(BALL_COLLISION_RADIUS + BALL_ARENA_CONTACT_BREAK);
+        const I3 lo = gridCell(center - ext);
+        const I3 hi = gridCell(center + ext);
+        const int nx = hi.x - lo.x + 1, ny = hi.y - lo.y + 1, nz = hi.z - lo.z + 1;
+        const int nCells = nx * ny * nz;
+        int& hitCount = wbuf[WARP_HIT_BUF];
+        if (lane == 0) hitCount = 0;
+        __syncwarp();
+        for (int q = 0; q < nCells; q++)
+        {
+            const int x = lo.x + q % nx, y = lo.y + (q / nx) % ny, z = lo.z + q / (nx * ny);
+            const int cell = flatCell(I3{ x, y, z });
+            const int start = __ldg(&arena.cellStart[cell]);
+            const int end = __ldg(&arena.cellStart[cell + 1]);
+            for (int e = start + lane; e < end; e += 32)
+            {
+                const int tri = __ldg(&arena.cellTris[e]);
+                V3 v0, v1, v2;
+                int flags;
+                loadTri(arena, tri, v0, v1, v2, flags);
+                BallContact c;
+                if (sphereTriangle(center, BALL_COLLISION_RADIUS, v0, v1, v2, c))
+                {
+                    const int slot = atomicAdd(&hitCount, 1);
+                    if (slot < WARP_HIT_BUF) wbuf[slot] = tri;
+                }
+            }
+        }
+        __syncwarp();
+
+        if (lane == 0)
+        {
+            BallContact set[4];
+            int count = 0;
+            const int n = hitCount;
+            if (n <= WARP_HIT_BUF)
+            {
+                // Ascending, de-duplicated triangle order (the reference merges the
+                // per-cell lists in triangle order and skips repeats).
+                for (int i = 1; i < n; i++)
+                {
+                    const int v = wbuf[i];
+                    int j = i - 1;
+                    while (j >= 0 && wbuf[j] > v)
+                    {
+                        wbuf[j + 1] = wbuf[j];
+                        j--;
+                    }
+                    wbuf[j + 1] = v;
+                }
+                int last = -1;
+                for (int i = 0; i < n; i++)
+                {
+                    const int tri = wbuf[i];
+                    if (tri == last) continue;
+                    last = tri;
+                    V3 v0, v1, v2;
+                    int flags;
+                    loadTri(arena, tri, v0, v1, v2, flags);
+                    BallContact c;
+                    sphereTriangle(center, BALL_COLLISION_RADIUS, v0, v1, v2, c);
+                    insertBallContact(set, count, c, center, v0, v1, v2, triAngles(arena, tri));
+                }
+            }
+            else
+            {
+                // Too many hits to buffer: walk the union of the cell lists in
+                // ascending triangle order directly.
+                int cursor = -1;
+                while (true)
+                {
+                    int next = 0x7fffffff;
+                    for (int q = 0; q < nCells; q++)
+                    {
+                        const int x = lo.x + q % nx, y = lo.y + (q / nx) % ny, z = lo.z + q / (nx * ny);
+                        const int cell = flatCell(I3{ x, y, z });
+                        for (int e = __ldg(&arena.cellStart[cell]); e < __ldg(&arena.cellStart[cell + 1]); e++)
+                        {
+                            const int tri = __ldg(&arena.cellTris[e]);
+                            if (tri > cursor)
+                            {
+                                if (tri < next) next = tri;
+                                break;  // cell lists are ascending
+                            }
+                        }
+                    }
+                    if (next == 0x7fffffff) break;
+                    cursor = next;
+                    V3 v0, v1, v2;
+                    int flags;
+                    loadTri(arena, next, v0, v1, v2, flags);
+                    BallContact c;
+                    if (sphereTriangle(center, BALL_COLLISION_RADIUS, v0, v1, v2, c))
+                        insertBallContact(set, count, c, center, v0, v1, v2, triAngles(arena, next));
+                }
+            }
+
+            bool wasHit = false;
+            for (int k = 0; k < nCars; k++)
+            {
+                const int hitTick = cars.n(C_BALL_HIT_TICK, carBase + k);
+                wasHit |= hitTick >= 0 && tick > 0 && hitTick == tick - 1;
+            }
+            BallBody body;
+            body.pos = center;
+            body.vel = preSolveVel;
+            body.velNoExt = velNoExt;
+            body.ang = ballAng;
+            body.deltaVel = body.deltaAng = body.pushVel = body.pushAng = v3zero();
+            solveBallArena(body, set, count, wasHit);
+            sims.setv(S_BVEL, s, body.vel);
+            sims.setv(S_BANG, s, body.ang);
+            pushVel = body.pushVel;
+        }
+    }
+    __syncwarp();
+
+    // Ball vs cars: distance gates across lanes (they use the pre-contact ball
+    // position), contacts in car order on lane 0.
+    bool gate = false;
+    if (lane < nCars)
+    {
+        const int i = carBase + lane;
+        gate = !cars.n(C_DEMOED, i) && ballCarGate(exportedPos, cars.v(C_CEN, i));
+    }
+    const unsigned gates = __ballot_sync(FULL, gate);
+    if (lane == 0)
+    {
+        for (unsigned m = gates; m; m &= m - 1)
+            solveBallCar(cars, carBase + __ffs(m) - 1, sims, s, preSolveVel, tick);
+
+        const V3 corrected = sims.v(S_BPOS, s);
+        if (lensq(corrected - exportedPos) != 0.f) posBT = corrected * .02f;
+        const V3 finalVel = sims.v(S_BVEL, s);
+        velBT = lensq(finalVel - preSolveVel) == 0.f ? preSolveBT : finalVel * .02f;
+        posBT = posBT + (pushVel * .02f) * PHYS_DT;
+        posBT = posBT + velBT * PHYS_DT;
+        const V3 ballPos = posBT * 50.f;
+        sims.setv(S_BPOS, s, ballPos);
+        sims.setv(S_IPOS, s, posBT);
+        sims.setv(S_IVEL, s, velBT);
+        sims.setv(S_EPOS, s, ballPos);
+        sims.setv(S_EVEL, s, finalVel);
+        sims.n(S_IVALID, s) = 1;
+        detectGoal(sims, s, ballPos, tick);
+    }
+    __syncwarp();
+}
+
+// ---- the kernel -------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(256) tickKernel(TickParams p, ArenaDev arena)
+{
+    extern __shared__ __align__(16) float smem[];
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const int nCars = p.nCars;
+    const Layout L = layoutOf(p.tileSims, nCars, arena.hitWords, blockDim.x);
+    const int simBase = blockIdx.x * p.tileSims;
+    const int simsHere = min(p.tileSims, p.nSim - simBase);
+    const int carsHere = simsHere * nCars;
+    const long long carBase = (long long)simBase * nCars;
+
+    const SmemSoa cars{ smem + L.cw, L.TC };
+    const SmemSoa sims{ smem + L.sw, L.TS };
+    int* cellS = reinterpret_cast<int*>(smem + L.cell);
+    int* cntS = reinterpret_cast<int*>(smem + L.cnt);
+    int* preS = reinterpret_cast<int*>(smem + L.pre);
+    float* rsS = smem + L.rs;
+    unsigned* hitS = reinterpret_cast<unsigned*>(smem + L.hits);
+    int* wsumS = reinterpret_cast<int*>(smem + L.wsum);
+    unsigned long long* keyS = reinterpret_cast<unsigned long long*>(smem + L.key);
+    int* wbuf = reinterpret_cast<int*>(smem + L.warp) + warp * WARP_WORDS;
+
+    // ---- load the tile ----
+    for (int w = 0; w < NCW; w++)
+        for (int i = tid; i < carsHere; i += blockDim.x)
+            cars.f(w, i) = p.car[(long long)w * p.carStride + carBase + i];
+    for (int w = 0; w < NSW; w++)
+        for (int i = tid; i < simsHere; i += blockDim.x)
+            sims.f(w, i) = p.sim[(long long)w * p.simStride + simBase + i];
+
+    const bool carThread = tid < carsHere;
+    const int mySim = carThread ? tid / nCars : 0;
+    const int myLocal = carThread ? tid - mySim * nCars : 0;
+    Controls ctl{};
+    if (carThread) ctl = decodeAction(p.actions, p.actionKind, carBase + tid);
+    unsigned wheelContactBits = 0;
+    bool respawned = false;
+    __syncthreads();
+
+    for (int t = 0; t < p.nTicks; t++)
+    {
+        const int tick = p.tick0 + t + 1;
+        const bool lastTick = t == p.nTicks - 1;
+
+        // ---- begin step + broadphase ----
+        if (tid < simsHere) sims.n(S_EP_TICKS, tid) += 1;
+        if (carThread)
+        {
+            const V3 pos = cars.v(C_POS, tid), vel = cars.v(C_VEL, tid), ang = cars.v(C_ANG, tid);
+            const V3 cen = cars.v(C_CEN, tid);
+            const Q4 rot = cars.q(C_ROT, tid);
+            const int cell = broadphaseCell(pos, vel, ang, cen, rot);
+            cellS[tid] = cell;
+            cntS[tid] = __ldg(&arena.cellStart[cell + 1]) - __ldg(&arena.cellStart[cell]);
+            const V3 up = rotate(rot, axisVec(2));
+            #pragma unroll
+            for (int w = 0; w < NUM_WHEELS; w++)
+            {
+                const V3 st = cen + rotate(rot, suspConnection(w));
+                rsS[(3 * w) * L.TC + tid] = st.x;
+                rsS[(3 * w + 1) * L.TC + tid] = st.y;
+                rsS[(3 * w + 2) * L.TC + tid] = st.z;
+                keyS[4 * tid + w] = rayKey(rayLen(w) + 1.f, 0xffffffffu);
+            }
+            const V3 dir = neg(up);
+            rsS[12 * L.TC + tid] = dir.x;
+            rsS[13 * L.TC + tid] = dir.y;
+            rsS[14 * L.TC + tid] = dir.z;
+            for (int h = 0; h < L.HW; h++) hitS[h * L.TC + tid] = 0u;
+        }
+        else if (tid < L.TC)
+        {
+            cntS[tid] = 0;
+        }
+
+        // ---- block exclusive scan of candidate counts ----
+        {
+            int v = tid < carsHere ? cntS[tid] : 0;
+            #pragma unroll
+            for (int d = 1; d < 32; d <<= 1)
+            {
+                const int u = __shfl_up_sync(FULL, v, d);
+                if (lane >= d) v += u;
+            }
+            if (lane == 31) wsumS[warp] = v;
+            __syncthreads();
+            if (warp == 0)
+            {
+                int s = lane < L.W ? wsumS[lane] : 0;
+                #pragma unroll
+                for (int d = 1; d < 32; d <<= 1)
+                {
+                    const int u = __shfl_up_sync(FULL, s, d);
+                    if (lane >= d) s += u;
+                }
+                if (lane < L.W) wsumS[lane] = s;
+            }
+            __syncthreads();
+            if (warp > 0) v += wsumS[warp - 1];
+            if (tid < carsHere) preS[tid + 1] = v;
+            if (tid == 0) preS[0] = 0;
+        }
+        __syncthreads();
+
+        // ---- flattened (car, candidate) work: wheel rays and SAT ----
+        const int total = preS[carsHere];
+        for (int it = tid; it < total; it += blockDim.x)
+        {
+            int lo = 0, hi = carsHere - 1;
+            while (lo < hi)
+            {
+                const int mid = (lo + hi + 1) >> 1;
+                if (preS[mid] <= it) lo = mid;
+                else hi = mid - 1;
+            }
+            const int c = lo;
+            const int k = it - preS[c];
+            const int tri = __ldg(&arena.cellTris[__ldg(&arena.cellStart[cellS[c]]) + k]);
+            V3 v0, v1, v2;
+            int flags;
+            loadTri(arena, tri, v0, v1, v2, flags);
+
+            // Wheel rays (Moller-Trumbore).
+            const V3 dir = { rsS[12 * L.TC + c], rsS[13 * L.TC + c], rsS[14 * L.TC + c] };
+            const V3 e1 = v1 - v0;
+            const V3 e2 = v2 - v0;
+            const V3 pv = cross(dir, e2);
+            const float det = dot(e1, pv);
+            if (!(fabsf(det) < RAY_PARALLEL_EPS))
+            {
+                const float invDet = 1.f / det;
+                #pragma unroll
+                for (int w = 0; w < NUM_WHEELS; w++)
+                {
+                    const V3 st = { rsS[(3 * w) * L.TC + c], rsS[(3 * w + 1) * L.TC + c], rsS[(3 * w + 2) * L.TC + c] };
+                    const V3 tv = st - v0;
+                    const float u = invDet * dot(tv, pv);
+                    if (u < 0.f || u > 1.f) continue;
+                    const V3 qv = cross(tv, e1);
+                    const float v = invDet * dot(dir, qv);
+                    if (v < 0.f || u + v > 1.f) continue;
+                    const float dist = invDet * dot(e2, qv);
+                    if (dist <= 0.f || !(dist < rayLen(w) + 1.f)) continue;
+                    atomicMin(&keyS[4 * c + w], rayKey(dist, (unsigned)k));
+                }
+            }
+
+            // Car-vs-triangle SAT (analytic planes are handled by the manifold).
+            if (!(flags & 1))
+            {
+                const LocalTri lt = localTriangle(cars.v(C_CEN, c), cars.q(C_ROT, c), v0, v1, v2);
+                if (carTriSat(lt).overlap) atomicOr(&hitS[(k >> 5) * L.TC + c], 1u << (k & 31));
+            }
+        }
+        __syncthreads();
+
+        // ---- per car: finish wheel rays, controls ----
+        float rayDist[NUM_WHEELS];
+        V3 rayNormal[NUM_WHEELS];
+        if (carThread)
+        {
+            const int i = tid;
+            const V3 cen = cars.v(C_CEN, i);
+            const Q4 rot = cars.q(C_ROT, i);
+            const V3 up = rotate(rot, axisVec(2));
+            const V3 dir = neg(up);
+            int src[NUM_WHEELS];
+            V3 start[NUM_WHEELS];
+            const int cellFirst = __ldg(&arena.cellStart[cellS[i]]);
+            #pragma unroll
+            for (int w = 0; w < NUM_WHEELS; w++)
+            {
+                start[w] = V3{ rsS[(3 * w) * L.TC + i], rsS[(3 * w + 1) * L.TC + i], rsS[(3 * w + 2) * L.TC + i] };
+                const unsigned long long key = keyS[4 * i + w];
+                const unsigned cand = (unsigned)(key & 0xffffffffu);
+                if (cand != 0xffffffffu)
+                {
+                    rayDist[w] = __uint_as_float((unsigned)(key >> 32));
+                    V3 v0, v1, v2;
+                    int flags;
+                    loadTri(arena, __ldg(&arena.cellTris[cellFirst + (int)cand]), v0, v1, v2, flags);
+                    V3 n = cross(v1 - v0, v2 - v0);
+                    const float nl = lensq(n);
+                    n = n * rsqrtf(nl);
+                    if (dot(n, dir) > 0.f) n = neg(n);
+                    rayNormal[w] = n;
+                    src[w] = WHEEL_ARENA;
+                }
+                else
+                {
+                    rayDist[w] = rayLen(w) + 1.f;
+                    rayNormal[w] = up;
+                    src[w] = WHEEL_NONE;
+                }
+            }
+            // Other cars' boxes, in car order.
+            const int sb = mySim * nCars;
+            for (int k = 0; k < nCars; k++)
+            {
+                const int o = sb + k;
+                if (o == i || cars.n(C_DEMOED, o)) continue;
+                const V3 oc = cars.v(C_CEN, o);
+                if (lensq(oc - cen) > 250.f * 250.f) continue;  // beyond any wheel ray + box reach
+                const Q4 orot = cars.q(C_ROT, o);
+                #pragma unroll
+                for (int w = 0; w < NUM_WHEELS; w++)
+                {
+                    const V3 ls = unrotate(orot, start[w] - oc);
+                    const V3 ld = unrotate(orot, dir);
+                    float entry = 0.f, exitD = rayLen(w);
+                    int hitAxis = -1;
+                    bool miss = false;
+                    #pragma unroll
+                    for (int a = 0; a < 3; a++)
+                    {
+                        const float h = vget(carHalfExtents(), a);
+                        const float d = vget(ld, a), s0 = vget(ls, a);
+                        if (fabsf(d) < RAY_PARALLEL_EPS)
+                        {
+                            if (fabsf(s0) > h) { miss = true; break; }
+                            continue;
+                        }
+                        const float inv = 1.f / d;
+                        const float t1 = (-h - s0) * inv;
+                        const float t2 = (h - s0) * inv;
+                        const float tn = fminf(t1, t2);
+                        if (tn > entry)
+                        {
+                            entry = tn;
+                            hitAxis = a;
+                        }
+                        exitD = fminf(exitD, fmaxf(t1, t2));
+                        if (entry > exitD) { miss = true; break; }
+                    }
+                    if (miss || hitAxis < 0 || entry >= rayDist[w]) continue;
+                    V3 ln = v3zero();
+                    vset(ln, hitAxis, vget(ld, hitAxis) > 0.f ? -1.f : 1.f);
+                    rayDist[w] = entry;
+                    rayNormal[w] = rotate(orot, ln);
+                    src[w] = WHEEL_CAR;
+                }
+            }
+            // Ball.
+            {
+                const V3 bp = sims.v(S_BPOS, mySim);
+                const float invR = 1.f / BALL_COLLISION_RADIUS;
+                #pragma unroll
+                for (int w = 0; w < NUM_WHEELS; w++)
+                {
+                    const V3 off = start[w] - bp;
+                    const float b = dot(off, dir);
+                    const float cc = lensq(off) - BALL_COLLISION_RADIUS * BALL_COLLISION_RADIUS;
+                    if (cc < 0.f) continue;
+                    const float disc = b * b - cc;
+                    if (disc < 0.f) continue;
+                    const float dist = -b - sqrtf(disc);
+                    if (!(dist > 0.f && dist <= rayLen(w))) continue;
+                    if (dist >= rayDist[w]) continue;
+                    rayDist[w] = dist;
+                    rayNormal[w] = (start[w] + dir * dist - bp) * invR;
+                    src[w] = WHEEL_BALL;
+                }
+            }
+            wheelContactBits = 0;
+            #pragma unroll
+            for (int w = 0; w < NUM_WHEELS; w++)
+                if (src[w] != WHEEL_NONE && rayDist[w] <= rayLen(w)) wheelContactBits |= 1u << w;
+            if (lastTick)
+            {
+                #pragma unroll
+                for (int w = 0; w < NUM_WHEELS; w++)
+                {
+                    const long long g = carBase + i;
+                    p.carOut[(long long)(O_RAY_DIST + w) * p.carStride + g] = rayDist[w];
+                    p.carOut[(long long)(O_RAY_NORMAL + 3 * w) * p.carStride + g] = rayNormal[w].x;
+                    p.carOut[(long long)(O_RAY_NORMAL + 3 * w + 1) * p.carStride + g] = rayNormal[w].y;
+                    p.carOut[(long long)(O_RAY_NORMAL + 3 * w + 2) * p.carStride + g] = rayNormal[w].z;
+                    reinterpret_cast<int*>(p.carOut)[(long long)(O_WHEEL_SRC + w) * p.carStride + g] = src[w];
+                }
+            }
+
+            // Controls.
+            V3 vel = cars.v(C_VEL, i), ang = cars.v(C_ANG, i);
+            Internal s = loadInternal(cars, i);
+            Susp su = loadSusp(cars, i);
+            processControls(ctl, cars.n(C_DEMOED, i) != 0, rot, vel, ang, s, su, rayDist,
+                            cars.n(C_MAN_COUNT, i), cars.v(C_MAN_N0, i));
+            cars.setv(C_VEL, i, vel);
+            cars.setv(C_ANG, i, ang);
+            storeInternal(cars, i, s);
+            storeSusp(cars, i, su);
+        }
+        __syncthreads();  // every ray has read the other cars' poses
+
+        // ---- per car: SAT contacts, suspension, manifold, solve ----
+        if (carThread)
+        {
+            const int i = tid;
+            const V3 cen = cars.v(C_CEN, i);
+            const Q4 rot = cars.q(C_ROT, i);
+            const int cellFirst = __ldg(&arena.cellStart[cellS[i]]);
+            const int nCand = cntS[i];
+
+            if (lastTick && p.diagCar)
+            {
+                const long long g = carBase + i;
+                p.diagCar[0 * p.carStride + g] = cellS[i];
+                p.diagCar[1 * p.carStride + g] = nCand;
+                int nh = 0;
+                for (int h = 0; h < L.HW && nh < MAX_CAR_TRI_PAIRS; h++)
+                    for (unsigned m = hitS[h * L.TC + i]; m && nh < MAX_CAR_TRI_PAIRS; m &= m - 1)
+                    {
+                        const int k = h * 32 + __ffs(m) - 1;
+                        p.diagCar[(3 + nh) * p.carStride + g] = __ldg(&arena.cellTris[cellFirst + k]);
+                        nh++;
+                    }
+                p.diagCar[2 * p.carStride + g] = nh;
+                for (int r = nh; r < MAX_CAR_TRI_PAIRS; r++) p.diagCar[(3 + r) * p.carStride + g] = -1;
+            }
+
+            if (!cars.n(C_DEMOED, i))
+            {
+                Body body = loadCarBody(cars, i);
+                Susp su = loadSusp(cars, i);
+                float lat[NUM_WHEELS], lon[NUM_WHEELS];
+                #pragma unroll
+                for (int w = 0; w < NUM_WHEELS; w++)
+                {
+                    lat[w] = cars.f(C_LAT + w, i);
+                    lon[w] = cars.f(C_LON + w, i);
+                }
+                applySuspension(body, su, lat, lon, rayDist, rayNormal, cars.n(C_MAN_COUNT, i),
+                                cars.v(C_MAN_N0, i), tick, (p.compatFlags & 1) != 0);
+
+                MPoint pts[MAX_CAR_MANIFOLD_POINTS];
+                int count = planeManifold(cen, rot, pts);
+                const int planeCount = count;
+
+                // Best mesh contact over the first MAX_CAR_TRI_PAIRS SAT hits.
+                Contact best{};
+                float bestDist = 3.402823466e+38f;
+                int bestTri = -1;
+                int seen = 0;
+                for (int h = 0; h < L.HW && seen < MAX_CAR_TRI_PAIRS; h++)
+                {
+                    for (unsigned m = hitS[h * L.TC + i]; m && seen < MAX_CAR_TRI_PAIRS; m &= m - 1)
+                    {
+                        seen++;
+                        const int k = h * 32 + __ffs(m) - 1;
+                        const int tri = __ldg(&arena.cellTris[cellFirst + k]);
+                        V3 v0, v1, v2;
+                        int flags;
+                        loadTri(arena, tri, v0, v1, v2, flags);
+                        const LocalTri lt = localTriangle(cen, rot, v0, v1, v2);
+                        const Sat sat = carTriSat(lt);
+                        pairContacts(lt, sat, [&](const Contact& c) {
+                            if (nearManifoldPoint(pts, planeCount, c.carPos)) return;
+                            const float d = -c.depth;
+                            if (d < bestDist)
+                            {
+                                bestDist = d;
+                                best = c;
+                                bestTri = tri;
+                            }
+                        });
+                    }
+                }
+                if (bestTri >= 0)
+                {
+                    V3 v0, v1, v2;
+                    int flags;
+                    loadTri(arena, bestTri, v0, v1, v2, flags);
+                    adjustInternalEdge(localTriangle(cen, rot, v0, v1, v2), triAngles(arena, bestTri), best);
+                    addManifoldPoint(pts, count, contactToManifold(best, cen, rot));
+                }
+
+                if (count > 0)
+                {
+                    solveCarManifold(body, pts, count);
+                    integrateSplitCorrection(body);
+                }
+                cars.n(C_MAN_COUNT, i) = count;
+                cars.setv(C_MAN_N0, i, count > 0 ? pts[0].worldNormal : v3zero());
+                body.vel = body.vel + body.extVel + body.deltaVel;
+                body.ang = body.ang + body.extAng + body.deltaAng;
+                storeCarBody(cars, i, body);
+                storeSusp(cars, i, su);
+                #pragma unroll
+                for (int w = 0; w < NUM_WHEELS; w++)
+                {
+                    cars.f(C_LAT + w, i) = lat[w];
+                    cars.f(C_LON + w, i) = lon[w];
+                }
+            }
+        }
+        __syncthreads();
+
+        // ---- per sim (one warp each): car-car pairs, then the ball ----
+        for (int s = warp; s < simsHere; s += L.W)
+        {
+            const int sb = s * nCars;
+            const int nPairs = nCars * (nCars - 1) / 2;
+            bool gate = false;
+            int pa = 0, pb = 0;
+            if (lane < nPairs)
+            {
+                int q = lane;
+                for (int a = 0; a < nCars - 1; a++)
+                {
+                    const int span = nCars - 1 - a;
+                    if (q < span)
+                    {
+                        pa = a;
+                        pb = a + 1 + q;
+                        break;
+                    }
+                    q -= span;
+                }
+                gate = carCarGate(cars, sb + pb, sb + pa);
+            }
+            const unsigned anyGate = __ballot_sync(FULL, gate);
+            if (anyGate && lane == 0)
+            {
+                SimCars<SmemSoa> sc{ cars, sb, nCars, p.nBlue, (int)(p.globalCarBase + carBase + sb), tick, p.seed };
+                int pair = 0;
+                for (int a = 0; a < nCars - 1; a++)
+                    for (int b = a + 1; b < nCars; b++, pair++)
+                    {
+                        const int kept = solveCarCarPair(sc, b, a);
+                        if (lastTick && p.diagSim && pair < DIAG_SIM_WORDS)
+                            p.diagSim[pair * p.simStride + simBase + s] = kept;
+                    }
+            }
+            else if (!anyGate && lastTick && p.diagSim && lane < nPairs && lane < DIAG_SIM_WORDS)
+            {
+                p.diagSim[lane * p.simStride + simBase + s] = 0;
+            }
+            __syncwarp();
+            ballStage(cars, sims, s, nCars, tick, arena, wbuf, lane);
+        }
+        __syncthreads();
+
+        // ---- per car: integrate, finish tick; per sim: finish ball ----
+        if (carThread)
+        {
+            const int i = tid;
+            if (!cars.n(C_DEMOED, i))
+            {
+                V3 pos = cars.v(C_POS, i), cen, vel = cars.v(C_VEL, i), ang = cars.v(C_ANG, i);
+                Q4 rot = cars.q(C_ROT, i);
+                integratePose(pos, cen, rot, vel, ang);
+                clampCarVelocity(vel, ang);
+                cars.setv(C_POS, i, pos);
+                cars.setv(C_VEL, i, vel);
+                cars.setv(C_ANG, i, ang);
+                cars.setv(C_CEN, i, cen);
+                cars.setq(C_ROT, i, rot);
+            }
+            if (finishCar(cars, i, ctl.steer, myLocal >= p.nBlue, c_tables)) respawned = true;
+        }
+        if (tid < simsHere) finishBall(sims, tid);
+        __syncthreads();
+
+        // ---- boost pads ----
+        for (int it = tid; it < simsHere * NUM_BOOST_PADS; it += blockDim.x)
+        {
+            const int s = it / NUM_BOOST_PADS;
+            boostPad(cars, s * nCars, nCars, sims, s, it - s * NUM_BOOST_PADS, c_tables);
+        }
+        __syncthreads();
+
+        if (lastTick && carThread)
+        {
+            const long long g = carBase + tid;
+            int* outI = reinterpret_cast<int*>(p.carOut);
+            #pragma unroll
+            for (int w = 0; w < NUM_WHEELS; w++)
+                outI[(long long)(O_WHEEL_CON + w) * p.carStride + g] = respawned ? 0 : (int)((wheelContactBits >> w) & 1u);
+        }
+        respawned = false;
+    }
+
+    // ---- store the tile ----
+    if (carThread)
+    {
+        const long long g = carBase + tid;
+        p.carOut[(long long)(O_CONTROLS + 0) * p.carStride + g] = ctl.throttle;
+        p.carOut[(long long)(O_CONTROLS + 1) * p.carStride + g] = ctl.steer;
+        p.carOut[(long long)(O_CONTROLS + 2) * p.carStride + g] = ctl.yaw;
+        p.carOut[(long long)(O_CONTROLS + 3) * p.carStride + g] = ctl.pitch;
+        p.carOut[(long long)(O_CONTROLS + 4) * p.carStride + g] = ctl.roll;
+        int* outI = reinterpret_cast<int*>(p.carOut);
+        outI[(long long)(O_CONTROLS + 5) * p.carStride + g] = ctl.jump;
+        outI[(long long)(O_CONTROLS + 6) * p.carStride + g] = ctl.boost;
+        outI[(long long)(O_CONTROLS + 7) * p.carStride + g] = ctl.slide;
+    }
+    for (int w = 0; w < NCW; w++)
+        for (int i = tid; i < carsHere; i += blockDim.x)
+            p.car[(long long)w * p.carStride + carBase + i] = cars.f(w, i);
+    for (int w = 0; w < NSW; w++)
+        for (int i = tid; i < simsHere; i += blockDim.x)
+            p.sim[(long long)w * p.simStride + simBase + i] = sims.f(w, i);
+}
+
+}  // namespace
+
+int uploadTickTables(const Tables& t)
+{
+    return (int)cudaMemcpyToSymbol(c_tables, &t, sizeof(Tables));
+}
+
+int tickThreads(int tileSims, int nCars)
+{
+    const int cars = tileSims * nCars;
+    return ((cars + 31) / 32) * 32;
+}
+
+size_t tickSmemBytes(int tileSims, int nCars, int hitWords, int threads)
+{
+    return (size_t)layoutOf(tileSims, nCars, hitWords, threads).total * 4;
+}
+
+int launchTick(const TickParams& p, const ArenaDev& a, void* stream)
+{
+    if (p.nTicks <= 0 || p.nSim <= 0) return 0;
+    const int threads = tickThreads(p.tileSims, p.nCars);
+    const size_t smem = tickSmemBytes(p.tileSims, p.nCars, a.hitWords, threads);
+    static bool configured = false;
+    if (!configured)
+    {
+        cudaFuncSetAttribute(tickKernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        configured = true;
+    }
+    const int blocks = (p.nSim + p.tileSims - 1) / p.tileSims;
+    tickKernel<<<blocks, threads, smem, (cudaStream_t)stream>>>(p, a);
+    return (int)cudaGetLastError();
+}
+
+}  // namespace cb

@@ -1,0 +1,51 @@
+// Launch-side description of the fused tick kernel and the device arena.
+#pragma once
+
+#include <cstdint>
+
+#include "cb_state.cuh"
+
+namespace cb {
+
+// Action encodings (numbering of carlb_action_kind).
+enum ActionKind : int { ACT_DISCRETE = 0, ACT_CONTINUOUS = 1, ACT_DIRECT = 2 };
+
+struct ArenaDev
+{
+    const float4* triV;     // [nTris * 3]: vertices; .w of vertex 0 holds the TRI_* flag bits
+    const float4* triAng;   // [nTris]: signed edge angles (edge i = v_i -> v_(i+1)%3)
+    const int* cellStart;   // [NUM_CELLS + 1]
+    const int* cellTris;    // [cellStart[NUM_CELLS]]
+    int hitWords;           // ceil(max triangles per cell / 32)
+};
+
+struct TickParams
+{
+    float* car;             // [NCW][carStride]
+    float* sim;             // [NSW][simStride]
+    float* carOut;          // [NOW][carStride]
+    int* diagCar;           // optional [DIAG_CAR_WORDS][carStride]
+    int* diagSim;           // optional [DIAG_SIM_WORDS][simStride]
+    const void* actions;    // [nCars total][7] (8 words for direct controls)
+    long long carStride, simStride;
+    long long globalCarBase;  // env-global index of this env's car 0
+    int actionKind;
+    int nSim, nCars, nBlue, seed;
+    int tick0;              // tick count before the first tick of this launch
+    int nTicks;
+    int tileSims;           // sims per CTA
+    int compatFlags;        // carlb_config::compat_flags
+};
+
+struct Tables;
+// Copies the game tables into this kernel's constant memory.
+int uploadTickTables(const Tables& t);
+
+// Shared-memory bytes of one CTA of the tick kernel.
+size_t tickSmemBytes(int tileSims, int nCars, int hitWords, int threads);
+int tickThreads(int tileSims, int nCars);
+
+// Launches ceil(nSim / tileSims) CTAs on `stream`.
+int launchTick(const TickParams& p, const ArenaDev& a, void* stream);
+
+}  // namespace cb

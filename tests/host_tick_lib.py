@@ -1,0 +1,89 @@
+"""ctypes wrapper of tests/host_tick (the product's physics compiled for the
+host, stepped serially in the kernel's stage order).  TEST INFRASTRUCTURE."""
+
+from __future__ import annotations
+
+import ctypes
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+from carl_b200 import capi
+
+ROOT = Path(__file__).resolve().parents[1]
+SRC = ROOT / "tests" / "host_tick" / "host_tick.cpp"
+LIB = ROOT / "tests" / "host_tick" / "_build" / "libhosttick.so"
+DEPS = [SRC, *sorted((ROOT / "carl_b200" / "csrc").glob("*.cuh")), *sorted((ROOT / "carl_b200" / "csrc").glob("*.hpp")),
+        ROOT / "carl_b200" / "csrc" / "arena.cpp", ROOT / "carl_b200" / "csrc" / "tables.cpp"]
+_lib = None
+
+
+def build() -> Path:
+    if not LIB.exists() or any(d.stat().st_mtime > LIB.stat().st_mtime for d in DEPS):
+        LIB.parent.mkdir(exist_ok=True)
+        subprocess.run(["g++", "-std=c++17", "-O2", "-ffp-contract=off", "-fPIC", "-shared", "-include", "algorithm",
+                        "-o", str(LIB), str(SRC), str(ROOT / "carl_b200/csrc/arena.cpp"),
+                        str(ROOT / "carl_b200/csrc/tables.cpp")], check=True)
+    return LIB
+
+
+def _load():
+    global _lib
+    if _lib is None:
+        lib = ctypes.CDLL(str(build()))
+        lib.hosttick_create.restype = ctypes.c_void_p
+        lib.hosttick_create.argtypes = [ctypes.c_char_p] + [ctypes.c_int] * 4
+        lib.hosttick_error.restype = ctypes.c_char_p
+        lib.hosttick_destroy.argtypes = [ctypes.c_void_p]
+        lib.hosttick_read_field.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+        lib.hosttick_write_field.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+        lib.hosttick_ticks.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+        _lib = lib
+    return _lib
+
+
+class HostTick:
+    def __init__(self, arena_path: str, n_sim: int, n_blue: int, n_orange: int, seed: int = 0):
+        self.lib = _load()
+        h = self.lib.hosttick_create(str(arena_path).encode(), n_sim, n_blue, n_orange, seed)
+        if not h:
+            raise RuntimeError(self.lib.hosttick_error().decode())
+        self.h = ctypes.c_void_p(h)
+        self.n_sim, self.n_cars = n_sim, n_blue + n_orange
+
+    def close(self):
+        if self.h:
+            self.lib.hosttick_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def field_shape(self, name):
+        from oracle_ref import _RefEnv
+        return _RefEnv.field_shape(self, name)
+
+    def read_field(self, name):
+        rows, width = self.field_shape(name)
+        out = np.zeros((rows, width), dtype=np.uint32)
+        assert self.lib.hosttick_read_field(self.h, capi.FIELD[name], out.ctypes.data) == 0
+        return out
+
+    def write_field(self, name, words):
+        rows, width = self.field_shape(name)
+        arr = np.ascontiguousarray(words).view(np.uint32).reshape(rows, width)
+        assert self.lib.hosttick_write_field(self.h, capi.FIELD[name], arr.ctypes.data) == 0
+
+    def snapshot(self):
+        return {n: self.read_field(n) for n in capi.PERSISTENT_FIELDS}
+
+    def restore(self, snap):
+        for n, w in snap.items():
+            self.write_field(n, w)
+
+    def ticks(self, controls: np.ndarray, n: int):
+        self.lib.hosttick_ticks(self.h, np.ascontiguousarray(controls).ctypes.data, n)

@@ -1,0 +1,78 @@
+"""Field-by-field comparison of snapshots from two implementations.
+
+Tolerance: fp32 values agree within 1e-4 relative or
+1e-3 absolute (uu, uu/s, rad/s, ...); integer words must be equal.
+TEST INFRASTRUCTURE.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from carl_b200 import capi
+
+REL_TOL = 1e-4
+ABS_TOL = 1e-3
+
+# Fields that depend on the order the reference's SAT kernel wins atomicAdd
+# slots (set semantics) or that it leaves uninitialised until first written.
+ORDER_FREE = {"DIAG_SAT_PAIRS"}
+
+
+def words_to_values(name: str, words: np.ndarray):
+    kinds = capi.field_kinds(name, words.shape[1])
+    f = words.view(np.float32)
+    i = words.view(np.int32)
+    is_int = np.array([k == "i" for k in kinds])
+    return f, i, is_int
+
+
+def compare_field(name: str, a: np.ndarray, b: np.ndarray) -> dict:
+    """Returns counts of exact / within-tolerance / failing words and rows."""
+    assert a.shape == b.shape, (name, a.shape, b.shape)
+    fa, ia, is_int = words_to_values(name, a)
+    fb, ib, _ = words_to_values(name, b)
+    exact = a == b
+    ok = exact.copy()
+    if (~is_int).any():
+        x, y = fa[:, ~is_int].astype(np.float64), fb[:, ~is_int].astype(np.float64)
+        close = np.abs(x - y) <= np.maximum(ABS_TOL, REL_TOL * np.maximum(np.abs(x), np.abs(y)))
+        close |= np.isnan(x) & np.isnan(y)
+        ok[:, ~is_int] |= close
+    bad_rows = np.where(~ok.all(axis=1))[0]
+    err = 0.0
+    if (~is_int).any():
+        d = np.abs(fa[:, ~is_int].astype(np.float64) - fb[:, ~is_int].astype(np.float64))
+        d = d[np.isfinite(d)]
+        err = float(d.max()) if d.size else 0.0
+    return {"words": a.size, "exact": int(exact.sum()), "ok": int(ok.sum()), "bad_rows": bad_rows,
+            "max_abs": err}
+
+
+def compare_sat_pairs(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """Rows whose SAT pair sets differ (order within a row is free)."""
+    ia, ib = a.view(np.int32), b.view(np.int32)
+    bad = []
+    for r in range(ia.shape[0]):
+        na, nb = ia[r, 0], ib[r, 0]
+        if na != nb or set(ia[r, 1:1 + na].tolist()) != set(ib[r, 1:1 + nb].tolist()):
+            bad.append(r)
+    return np.array(bad, dtype=np.int64)
+
+
+def compare_snapshots(a: dict, b: dict, fields=None) -> dict:
+    fields = fields or [f for f in a if f in b]
+    return {name: compare_field(name, a[name], b[name]) for name in fields}
+
+
+def summarize(report: dict) -> str:
+    lines = []
+    for name, r in report.items():
+        flag = "" if r["ok"] == r["words"] else "  <-- %d rows" % len(r["bad_rows"])
+        lines.append("%-26s exact %6.2f%%  ok %7.3f%%  max|d| %.3g%s" % (
+            name, 100.0 * r["exact"] / max(1, r["words"]), 100.0 * r["ok"] / max(1, r["words"]), r["max_abs"], flag))
+    return "\n".join(lines)
+
+
+def all_ok(report: dict) -> bool:
+    return all(r["ok"] == r["words"] for r in report.values())
