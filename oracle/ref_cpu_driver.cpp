@@ -458,6 +458,14 @@ int carlref_write_field(void* h, int field, const void* in)
     return 0;
 }
 
+/* The reference's kickoff permutation table (src/RLConstants.cu:4-29). */
+int carlref_kickoff_table(int* out)
+{
+    for (int r = 0; r < 120; r++)
+        for (int k = 0; k < 4; k++) out[4 * r + k] = KICKOFF_PERMUTATIONS[r][k];
+    return 0;
+}
+
 /* Arena tables for the arena-build parity test. */
 int carlref_arena_sizes(void* h, int* sizes)
 {
