@@ -1,0 +1,392 @@
+"""Throughput benchmark of the batched Rocket League tick on B200.
+
+Workload (config C3): 3v3, n_sim = 32768 sims per GPU, default arena, seeded
+synthetic initial states (cars uniform over the field floor, planar velocity
+N(0, 800 uu/s), yaw uniform, boost U[0, 100], ball at rest at centre) and
+direct controls redrawn every 8 ticks (throttle/steer/pitch/yaw/roll U[-1, 1],
+jump/boost/handbrake Bernoulli(0.3)).
+
+A *step* is one control period: the controls for all cars are staged and 8
+physics ticks run (one launch of the fused tick kernel).  The metric is
+agent-steps/s = cars x ticks / s, one agent-step being one car advanced one
+120 Hz tick.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+For N > 1 it runs under torch.distributed.run, one rank per GPU; each rank
+simulates its own contiguous slice of sims (global sim offset rank*n_sim), so
+per-GPU work is fixed (weak scaling) and there is no collective in the tick.
+
+Timed region: barrier + synchronize, K steps, synchronize + barrier.  Each
+step's device time is taken with CUDA events on the env stream; between timed
+steps a 256 MiB buffer is written to flush the 126 MB L2 (outside the events).
+The roofline uses the tick kernel's own event time, read back per launch.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+
+TICKS_PER_STEP = 8
+FLUSH_BYTES = 256 << 20
+# Byte model CARLB-v1: persistent tick state read once and written once per
+# tick, packed fp32 (vec3 12 B, quat 16 B, ints 4 B), plus the actions read.
+BYTES_PER_CAR_TICK = 620
+BYTES_PER_SIM_TICK = 504
+METRIC = "agent-steps/sec at 3v3 n_sim=32768"
+UNIT = "agent-steps/s"
+
+
+def bytes_per_agent_tick(n_cars: int) -> float:
+    return (n_cars * BYTES_PER_CAR_TICK + BYTES_PER_SIM_TICK) / n_cars
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--n-sim", type=int, default=32768, help="sims per GPU")
+    ap.add_argument("--blue", type=int, default=3)
+    ap.add_argument("--orange", type=int, default=3)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------- clocks ----
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    QUERY = ("index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+
+    def __init__(self, device: int):
+        self.bus_id = ""
+        try:
+            import torch
+
+            pr = torch.cuda.get_device_properties(device)
+            self.bus_id = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        except Exception:
+            pass
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.25)
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.15)
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 10:
+                continue
+            if self.bus_id and f[1].lower()[-12:] != self.bus_id[-12:]:
+                continue
+            rows.append(f)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        mx = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
+        reasons = sorted({name for r in rows for name, v in zip(self.REASONS, r[6:10]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ------------------------------------------------------------ workload ----
+def make_env(args, rank: int, device: int):
+    from carl_b200 import capi, workloads
+
+    env = capi.Env(args.n_sim, args.blue, args.orange, seed=args.seed, device=device,
+                   sim_offset=rank * args.n_sim)
+    workloads.floor_state(env, args.seed + 1000 * rank)
+    return env
+
+
+def control_pool(n_cars_total: int, count: int, seed: int):
+    from carl_b200 import workloads
+
+    rng = np.random.default_rng(seed)
+    return [workloads.controls(rng, n_cars_total) for _ in range(count)]
+
+
+def traffic_per_launch() -> float | None:
+    """DRAM bytes per tick-kernel launch at this workload, from the committed ncu summary."""
+    path = ROOT / "profiles" / "tick_kernel_3v3_32768.md"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            return float(line.split(":", 1)[1].split()[0])
+    return None
+
+
+def measured_hbm_peak() -> tuple[float, str]:
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return float(peaks["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+# -------------------------------------------------------- reference CPU ----
+def reference_cpu_time(snapshot, n_sim, n_blue, n_orange, seed, controls, steps, threads):
+    """Times the reference's tick compiled for the host (OpenMP over sims).
+
+    Returns (agent-steps/s, seconds, threads used)."""
+    from oracle.refenv import RefCpu
+
+    used = RefCpu.set_threads(threads)
+    ref = RefCpu(n_sim, n_blue, n_orange, seed)
+    ref.restore(snapshot)
+    ref.ticks(2, controls[0], 1)  # touch pages / spin up the thread pool
+    t0 = time.perf_counter()
+    for i in range(steps):
+        ref.ticks(2, controls[i % len(controls)], TICKS_PER_STEP)
+    dt = time.perf_counter() - t0
+    ref.close()
+    return n_sim * (n_blue + n_orange) * TICKS_PER_STEP * steps / dt, dt, used
+
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# ------------------------------------------------------------- arms --------
+def run_reference(args, rank: int, world: int) -> None:
+    """The reference arm: the reference's own CPU tick on the host cores."""
+    if rank != 0:
+        return
+    from carl_b200 import capi, workloads
+
+    n_cars = args.blue + args.orange
+    # The initial state is built on the host restatement of the reference so the
+    # arm needs no GPU: kickoff reset, then the same seeded floor distribution.
+    from oracle.refenv import RefCpu
+
+    threads = host_threads()
+    RefCpu.set_threads(threads)
+    ref = RefCpu(args.n_sim, args.blue, args.orange, args.seed)
+    workloads.floor_state(ref, args.seed)
+    snap = ref.snapshot()
+    ref.close()
+    ctl = control_pool(args.n_sim * n_cars, 4, args.seed + 1)
+    steps = max(1, min(args.steps, 8))
+    warm = max(0, min(args.warmup, 1))
+    if warm:
+        reference_cpu_time(snap, args.n_sim, args.blue, args.orange, args.seed, ctl, warm, threads)
+    value, secs, used = reference_cpu_time(snap, args.n_sim, args.blue, args.orange, args.seed, ctl, steps, threads)
+    sample = (f"{steps} steps x {TICKS_PER_STEP} ticks of the full 3v3 n_sim={args.n_sim} workload "
+              f"({secs:.1f} s), OpenMP over sims")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps,
+        "warmup": warm, "ms_per_step": secs * 1e3 / steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded C3 floor states, direct controls)",
+        "config": {"workload": f"C3 {args.blue}v{args.orange} n_sim={args.n_sim}, direct controls held 8 ticks",
+                   "ticks_per_step": TICKS_PER_STEP, "implementation": "reference tick compiled for the host CPU"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": used, "kind": "reference", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_b200(args, rank: int, world: int, local_rank: int) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from carl_b200 import capi
+
+    device = local_rank
+    torch.cuda.set_device(device)
+    dev = torch.device("cuda", device)
+    n_cars = args.blue + args.orange
+    n_total_cars = args.n_sim * n_cars
+
+    env = make_env(args, rank, device)
+    stream = torch.cuda.ExternalStream(env.stream, device=dev)
+    pool_n = max(4, min(16, args.steps + args.warmup))
+    host_ctl = control_pool(n_total_cars, pool_n, args.seed + 1 + 7919 * rank)
+    dev_ctl = [torch.from_numpy(c.view(np.int32)).to(dev) for c in host_ctl]
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def step(i):
+        env.ticks(capi.ACTIONS_DIRECT, dev_ctl[i % pool_n], TICKS_PER_STEP)
+
+    snap0 = env.snapshot() if rank == 0 and not args.no_cpu_baseline and world == 1 else None
+
+    # ---- warm-up ----
+    for i in range(args.warmup):
+        step(i)
+    env.synchronize()
+
+    # ---- timed region ----
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    kernel_ms = []
+    sampler = ClockSampler(device)
+    sampler.start()
+    barrier()
+    torch.cuda.synchronize()
+    wall0 = time.perf_counter()
+    for i in range(args.steps):
+        with torch.cuda.stream(stream):
+            flush.fill_(i & 0xFF)
+            starts[i].record(stream)
+        step(args.warmup + i)
+        ends[i].record(stream)
+        env.synchronize()
+        kernel_ms.append(env.last_tick_ms())
+    torch.cuda.synchronize()
+    barrier()
+    wall = time.perf_counter() - wall0
+    clocks = sampler.stop()
+    step_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    kern_ms = sum(kernel_ms)
+
+    t = torch.tensor([step_ms, kern_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_ms, kern_ms = float(t[0]), float(t[1])
+
+    agent_ticks_rank = n_total_cars * TICKS_PER_STEP * args.steps
+    value = agent_ticks_rank * world / (step_ms / 1e3)
+
+    # ---- end to end through the C ABI with host buffers ----
+    e2e = None
+    if not args.no_e2e:
+        pinned_ctl = [torch.from_numpy(c).pin_memory() for c in host_ctl[: min(pool_n, 8)]]
+        rewards = torch.empty(args.n_sim, dtype=torch.float32).pin_memory()
+        for i in range(min(args.warmup, 3)):
+            env.ticks_host(capi.ACTIONS_DIRECT, pinned_ctl[i % len(pinned_ctl)].numpy(), TICKS_PER_STEP, rewards.numpy())
+        e_steps = max(1, min(args.steps, 50))
+        e0 = [torch.cuda.Event(enable_timing=True) for _ in range(e_steps)]
+        e1 = [torch.cuda.Event(enable_timing=True) for _ in range(e_steps)]
+        barrier()
+        torch.cuda.synchronize()
+        for i in range(e_steps):
+            with torch.cuda.stream(stream):
+                flush.fill_(i & 0xFF)
+                e0[i].record(stream)
+            env.ticks_host(capi.ACTIONS_DIRECT, pinned_ctl[i % len(pinned_ctl)].numpy(), TICKS_PER_STEP, rewards.numpy())
+            e1[i].record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ems = torch.tensor([sum(a.elapsed_time(b) for a, b in zip(e0, e1))], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+        e2e = {"value": n_total_cars * TICKS_PER_STEP * e_steps * world / (float(ems[0]) / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": int(host_ctl[0].nbytes), "d2h_bytes_per_step": int(rewards.numel() * 4),
+               "steps": e_steps, "path": "carlb_ticks_host (pinned host controls in, host rewards out)"}
+
+    if rank != 0:
+        env.close()
+        return
+
+    # ---- roofline of the fused tick kernel ----
+    peak, peak_kind = measured_hbm_peak()
+    bpat = bytes_per_agent_tick(n_cars)
+    launch_ms = kern_ms / args.steps
+    alg_bytes = bpat * n_total_cars * TICKS_PER_STEP
+    achieved = alg_bytes / (launch_ms / 1e3) / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "traffic": traffic_per_launch(), "peak_kind": peak_kind, "kernel": "tickKernel",
+                "launch_ms": launch_ms, "bytes_per_agent_tick": bpat,
+                "algorithmic_bytes_per_launch": alg_bytes}
+
+    cpu = None
+    if snap0 is not None:
+        secs_target = 12.0
+        threads = host_threads()
+        v, secs, used = reference_cpu_time(snap0, args.n_sim, args.blue, args.orange, args.seed, host_ctl, 1, threads)
+        more = int(max(0, min(16, secs_target / max(secs, 1e-3) - 1)))
+        steps_done, secs_tot = 1, secs
+        if more:
+            v, secs_tot, used = reference_cpu_time(snap0, args.n_sim, args.blue, args.orange, args.seed, host_ctl, more,
+                                                   threads)
+            steps_done = more
+        cpu = {"value": v, "unit": UNIT, "cores": used, "kind": "reference",
+               "sample": f"{steps_done} steps x {TICKS_PER_STEP} ticks of the same 3v3 n_sim={args.n_sim} workload "
+                         f"({secs_tot:.1f} s) with the reference tick compiled for the host, OpenMP over sims"}
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded C3 floor states, direct controls redrawn every 8 ticks)",
+        "config": {"workload": f"C3 {args.blue}v{args.orange} n_sim={args.n_sim} per GPU, direct controls held 8 ticks",
+                   "ticks_per_step": TICKS_PER_STEP, "sims_total": args.n_sim * world,
+                   "parallelism": f"sim-sharded x{world}", "l2": "256 MiB buffer written between timed steps",
+                   "wall_s": wall},
+        "clocks": clocks, "e2e": e2e, "gpu_launches": args.steps, "roofline": roofline, "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+    env.close()
+
+
+def main():
+    args = parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_b200(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -502,6 +502,7 @@ carlb_status carlb_apply_reset_state(carlb_env* e, int32_t n, const float* ballP
 {
     if (!e) return fail(nullptr, CARLB_ERR_VALUE, "env is null");
     if (mask && indices) return fail(e, CARLB_ERR_VALUE, "specify reset_mask or simulation_indices, not both");
+    if (mask && indices) return fail(e, CARLB_ERR_VALUE, "specify reset_mask or simulation_indices, not both");
     if (mask) n = e->cfg.n_sim;
     if (n < 0 || n > e->cfg.n_sim) return fail(e, CARLB_ERR_VALUE, "too many simulation_indices");
     if (!ballPos || !ballVel || !ballAng || !carPos || !carRot || !carVel || !carAng || !demoed)

@@ -1,4 +1,4 @@
-"""Seeded synthetic states and controls for parity tests and the benchmark.
+"""Seeded synthetic workloads (states and controls) for the benchmark and the tests.
 
 States are written field by field into an env that was reset to kickoff, so
 every word of the snapshot is defined.  Vector math that feeds derived fields

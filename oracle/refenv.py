@@ -58,6 +58,9 @@ def _load(kind: str) -> ctypes.CDLL:
         lib.carlref_set_threads.argtypes = [i32]
         lib.carlref_repack.argtypes = [vp]
         lib.carlref_tick_partial.argtypes = [vp, i32, vp, i32]
+        lib.carlref_arena_sizes.argtypes = [vp, vp]
+        lib.carlref_arena_tables.argtypes = [vp] * 7
+        lib.carlref_kickoff_table.argtypes = [vp]
     else:
         lib.carlrefgpu_tick_partial.argtypes = [vp, i32, vp, i32]
         lib.carlrefgpu_time_ticks.argtypes = [vp, i32, vp, i32, ctypes.POINTER(ctypes.c_float)]
@@ -202,3 +205,23 @@ class RefGpu(_RefEnv):
         self._call("apply_reset_state", n_selected, *[_addr(a) for a in arrs], int(demoed_is_byte),
                    _addr(car_boost), _addr(car_internal_state), _addr(blue_score), _addr(orange_score),
                    _addr(episode_ticks), _addr(simulation_indices), _addr(reset_mask))
+
+
+def reference_arena_tables(ref: RefCpu) -> dict[str, np.ndarray]:
+    """The reference's arena tables (src/ArenaMesh.cu:15-125) from a RefCpu env."""
+    lib = _load("cpu")
+    sizes = np.zeros(4, dtype=np.int32)
+    lib.carlref_arena_sizes(ref.h, sizes.ctypes.data)
+    nv, nt, nc, nr = (int(x) for x in sizes)
+    out = {"verts": np.zeros((nv, 3), np.float32), "tris": np.zeros((nt, 3), np.int32),
+           "prefix": np.zeros(nc + 1, np.int32), "tri_idx": np.zeros(nr, np.int32),
+           "edge_angles": np.zeros((nt, 3), np.float32), "ball_tri_idx": np.zeros(nr, np.int32)}
+    lib.carlref_arena_tables(ref.h, *[out[k].ctypes.data for k in
+                                      ("verts", "tris", "prefix", "tri_idx", "edge_angles", "ball_tri_idx")])
+    return out
+
+
+def reference_kickoff_table() -> np.ndarray:
+    out = np.zeros((120, 4), dtype=np.int32)
+    _load("cpu").carlref_kickoff_table(out.ctypes.data)
+    return out

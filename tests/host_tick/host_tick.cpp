@@ -560,3 +560,42 @@ int hosttick_ticks(void* h, const uint32_t* controls, int ticks)
 }
 
 }  // extern "C"
+
+extern "C" {
+
+// Product arena build (carl_b200/csrc/arena.cpp) for the arena parity test:
+// sizes = {nVerts, nTris, nCells, nRefs}.
+int hosttick_arena_sizes(void* h, int* sizes)
+{
+    auto* e = static_cast<HostEnv*>(h);
+    sizes[0] = e->arena.nVerts();
+    sizes[1] = e->arena.nTris();
+    sizes[2] = (int)e->arena.cellStart.size() - 1;
+    sizes[3] = e->arena.cellStart.back();
+    return 0;
+}
+
+int hosttick_arena_tables(void* h, float* verts, int* tris, int* cellStart, int* cellTris, float* edgeAngles,
+                          float* normals, int* flags)
+{
+    auto* e = static_cast<HostEnv*>(h);
+    const ArenaHost& a = e->arena;
+    std::memcpy(verts, a.verts.data(), a.verts.size() * 4);
+    std::memcpy(tris, a.tris.data(), a.tris.size() * 4);
+    std::memcpy(cellStart, a.cellStart.data(), a.cellStart.size() * 4);
+    std::memcpy(cellTris, a.cellTris.data(), a.cellTris.size() * 4);
+    std::memcpy(edgeAngles, a.edgeAngles.data(), a.edgeAngles.size() * 4);
+    std::memcpy(normals, a.normals.data(), a.normals.size() * 4);
+    std::memcpy(flags, a.triFlags.data(), a.triFlags.size() * 4);
+    return 0;
+}
+
+}  // extern "C"
+
+extern "C" int hosttick_kickoff_table(void* h, int* out)
+{
+    auto* e = static_cast<HostEnv*>(h);
+    for (int r = 0; r < 120; r++)
+        for (int k = 0; k < 4; k++) out[4 * r + k] = e->T.kickoffPerm[r][k];
+    return 0;
+}

@@ -39,6 +39,9 @@ def _load():
         lib.hosttick_read_field.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
         lib.hosttick_write_field.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
         lib.hosttick_ticks.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+        lib.hosttick_arena_sizes.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+        lib.hosttick_arena_tables.argtypes = [ctypes.c_void_p] * 8
+        lib.hosttick_kickoff_table.argtypes = [ctypes.c_void_p] * 2
         _lib = lib
     return _lib
 
@@ -64,7 +67,7 @@ class HostTick:
             pass
 
     def field_shape(self, name):
-        from oracle_ref import _RefEnv
+        from oracle.refenv import _RefEnv
         return _RefEnv.field_shape(self, name)
 
     def read_field(self, name):
@@ -84,6 +87,25 @@ class HostTick:
     def restore(self, snap):
         for n, w in snap.items():
             self.write_field(n, w)
+
+    def arena_tables(self) -> dict[str, np.ndarray]:
+        """The product's arena tables (carl_b200/csrc/arena.cpp)."""
+        sizes = np.zeros(4, dtype=np.int32)
+        self.lib.hosttick_arena_sizes(self.h, sizes.ctypes.data)
+        nv, nt, nc, nr = (int(x) for x in sizes)
+        out = {"verts": np.zeros((nv, 3), np.float32), "tris": np.zeros((nt, 3), np.int32),
+               "prefix": np.zeros(nc + 1, np.int32), "tri_idx": np.zeros(nr, np.int32),
+               "edge_angles": np.zeros((nt, 3), np.float32), "normals": np.zeros((nt, 3), np.float32),
+               "flags": np.zeros(nt, np.int32)}
+        self.lib.hosttick_arena_tables(self.h, *[out[k].ctypes.data for k in
+                                                 ("verts", "tris", "prefix", "tri_idx", "edge_angles", "normals",
+                                                  "flags")])
+        return out
+
+    def kickoff_table(self) -> np.ndarray:
+        out = np.zeros((120, 4), dtype=np.int32)
+        self.lib.hosttick_kickoff_table(self.h, out.ctypes.data)
+        return out
 
     def ticks(self, controls: np.ndarray, n: int):
         self.lib.hosttick_ticks(self.h, np.ascontiguousarray(controls).ctypes.data, n)

@@ -45,7 +45,7 @@ def compare_field(name: str, a: np.ndarray, b: np.ndarray) -> dict:
         d = np.abs(fa[:, ~is_int].astype(np.float64) - fb[:, ~is_int].astype(np.float64))
         d = d[np.isfinite(d)]
         err = float(d.max()) if d.size else 0.0
-    return {"words": a.size, "exact": int(exact.sum()), "ok": int(ok.sum()), "bad_rows": bad_rows,
+    return {"words": a.size, "rows": a.shape[0], "exact": int(exact.sum()), "ok": int(ok.sum()), "bad_rows": bad_rows,
             "max_abs": err}
 
 
@@ -76,3 +76,13 @@ def summarize(report: dict) -> str:
 
 def all_ok(report: dict) -> bool:
     return all(r["ok"] == r["words"] for r in report.values())
+
+
+def bad_row_fraction(report: dict, rows: int) -> float:
+    """Share of the `rows` records (cars or sims) with any word outside tolerance,
+    over every field that has one row per record."""
+    bad = set()
+    for r in report.values():
+        if r["rows"] == rows:
+            bad.update(r["bad_rows"].tolist())
+    return len(bad) / rows
