@@ -204,7 +204,8 @@ def run_reference(args, rank: int, world: int) -> None:
     workloads.floor_state(ref, args.seed)
     snap = ref.snapshot()
     ref.close()
-    ctl = control_pool(args.n_sim * n_cars, 4, args.seed + 1)
+    pool_n = max(4, min(16, args.steps + args.warmup))
+    ctl = control_pool(args.n_sim * n_cars, pool_n, args.seed + 1)
     steps = max(1, min(args.steps, 8))
     warm = max(0, min(args.warmup, 1))
     if warm:
@@ -220,8 +221,36 @@ def run_reference(args, rank: int, world: int) -> None:
                    "ticks_per_step": TICKS_PER_STEP, "implementation": "reference tick compiled for the host CPU"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": used, "kind": "reference", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "cuda_build": reference_cuda_time(args, snap, ctl),
     }
     print(json.dumps(line), flush=True)
+
+
+def reference_cuda_time(args, snapshot, controls) -> dict | None:
+    """The reference's own CUDA build (compiled from its sources for sm_100a),
+    stepped through its RLEnvironment::step path with direct controls on the
+    same states and the same control sequence as the b200 arm; device time
+    from CUDA events around each step's ticks."""
+    try:
+        import torch
+
+        if not torch.cuda.is_available():
+            return None
+        from oracle.refenv import RefGpu
+    except Exception as exc:  # the CUDA build is optional for the CPU reference arm
+        return {"unavailable": str(exc)}
+    n_cars = args.blue + args.orange
+    ref = RefGpu(args.n_sim, args.blue, args.orange, args.seed)
+    ref.restore(snapshot)
+    for i in range(args.warmup):
+        ref.ticks(2, controls[i % len(controls)], TICKS_PER_STEP)
+    total = 0.0
+    for i in range(args.steps):
+        total += ref.time_ticks(2, controls[(args.warmup + i) % len(controls)], TICKS_PER_STEP)
+    ref.close()
+    return {"value": args.n_sim * n_cars * TICKS_PER_STEP * args.steps / (total / 1e3), "unit": UNIT,
+            "ms_per_step": total / args.steps, "steps": args.steps, "warmup": args.warmup,
+            "what": "reference CUDA build (its sources, nvcc sm_100a --fmad=false -rdc), same states and controls"}
 
 
 def run_b200(args, rank: int, world: int, local_rank: int) -> None:

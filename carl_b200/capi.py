@@ -149,6 +149,28 @@ class Env:
         self._lib.carlb_dims(self._h, dims)
         self.n_sim, self.n_cars, self.obs_dim, self.act_dim, self.state_dim = list(dims)
         self.device = device
+        self._ext_stream = None
+
+    def _order_after_torch(self, *inputs) -> None:
+        """Orders the env stream after the producer of torch CUDA inputs.
+
+        Device inputs are read on the env's own (non-blocking) stream; a torch
+        tensor may still be being written on torch's current stream, so the env
+        stream waits for it, as the reference's DLPack handoff
+        (``__dlpack__(stream=env_stream)``) does.  Each input is also recorded on
+        the env stream so torch's caching allocator does not hand its memory to
+        a new tensor before the env's reads of it have run."""
+        waited = False
+        for x in inputs:
+            if x is not None and getattr(x, "is_cuda", False):
+                import torch
+
+                if self._ext_stream is None:
+                    self._ext_stream = torch.cuda.ExternalStream(self.stream, device=x.device)
+                if not waited:
+                    self._ext_stream.wait_stream(torch.cuda.current_stream(x.device))
+                    waited = True
+                x.record_stream(self._ext_stream)
 
     def _check(self, st: int) -> None:
         if st != OK:
@@ -167,12 +189,14 @@ class Env:
 
     # ---- stepping ----
     def ticks(self, kind: int, actions, n_ticks: int) -> None:
+        self._order_after_torch(actions)
         self._check(self._lib.carlb_ticks(self._h, kind, _ptr(actions), n_ticks))
 
     def ticks_host(self, kind: int, host_actions: np.ndarray, n_ticks: int, host_rewards: np.ndarray | None = None) -> None:
         self._check(self._lib.carlb_ticks_host(self._h, kind, _ptr(host_actions), n_ticks, _ptr(host_rewards)))
 
     def env_step(self, kind: int, actions) -> None:
+        self._order_after_torch(actions)
         self._check(self._lib.carlb_env_step(self._h, kind, _ptr(actions)))
 
     def reset(self) -> None:
@@ -187,22 +211,27 @@ class Env:
                           episode_ticks=None, simulation_indices=None, reset_mask=None) -> None:
         args = [ball_position, ball_velocity, ball_angular_velocity, car_position, car_rotation, car_velocity,
                 car_angular_velocity, car_demoed]
+        self._order_after_torch(*args, car_boost, car_internal_state, blue_score, simulation_indices, reset_mask)
         self._check(self._lib.carlb_apply_reset_state(
             self._h, n_selected, *[_ptr(a) for a in args], int(demoed_is_byte), _ptr(car_boost),
             _ptr(car_internal_state), _ptr(blue_score), _ptr(orange_score), _ptr(episode_ticks),
             _ptr(simulation_indices), _ptr(reset_mask)))
 
     def set_ball(self, n, pos, vel, ang, indices=None) -> None:
+        self._order_after_torch(pos, vel, ang, indices)
         self._check(self._lib.carlb_set_ball(self._h, n, _ptr(pos), _ptr(vel), _ptr(ang), _ptr(indices)))
 
     def set_car(self, n, pos, rot, vel, ang, demoed, demoed_is_byte, boost=None, internal=None, indices=None) -> None:
+        self._order_after_torch(pos, rot, vel, ang, demoed, boost, internal, indices)
         self._check(self._lib.carlb_set_car(self._h, n, _ptr(pos), _ptr(rot), _ptr(vel), _ptr(ang), _ptr(demoed),
                                             int(demoed_is_byte), _ptr(boost), _ptr(internal), _ptr(indices)))
 
     def set_match_state(self, n, blue, orange, ticks, indices=None) -> None:
+        self._order_after_torch(blue, orange, ticks, indices)
         self._check(self._lib.carlb_set_match_state(self._h, n, _ptr(blue), _ptr(orange), _ptr(ticks), _ptr(indices)))
 
     def reset_boost_pads(self, n, indices=None) -> None:
+        self._order_after_torch(indices)
         self._check(self._lib.carlb_reset_boost_pads(self._h, n, _ptr(indices)))
 
     # ---- outputs / properties ----

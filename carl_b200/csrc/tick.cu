@@ -826,11 +826,16 @@ int launchTick(const TickParams& p, const ArenaDev& a, void* stream)
     if (p.nTicks <= 0 || p.nSim <= 0) return 0;
     const int threads = tickThreads(p.tileSims, p.nCars);
     const size_t smem = tickSmemBytes(p.tileSims, p.nCars, a.hitWords, threads);
-    static bool configured = false;
-    if (!configured)
+    // The shared-memory opt-in is a per-device function attribute.
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !configured[dev])
     {
-        cudaFuncSetAttribute(tickKernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        configured = true;
+        const cudaError_t err = cudaFuncSetAttribute(tickKernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                     227 * 1024);
+        if (err != cudaSuccess) return (int)err;
+        if (dev >= 0 && dev < 64) configured[dev] = true;
     }
     const int blocks = (p.nSim + p.tileSims - 1) / p.tileSims;
     tickKernel<<<blocks, threads, smem, (cudaStream_t)stream>>>(p, a);

@@ -60,8 +60,30 @@ def compare_sat_pairs(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     return np.array(bad, dtype=np.int64)
 
 
+# The ball's cached integration state is dead while BALL_INT_VALID is 0 (the
+# next tick rebuilds it from the exported pose, include/Physics/BallArena/
+# Solve.cuh:68-76); the reference leaves it uninitialised until then.
+BALL_CACHE = ("BALL_INT_POS", "BALL_INT_VEL", "BALL_EXP_POS", "BALL_EXP_VEL")
+
+
+def _mask_dead_ball_cache(a: dict, b: dict) -> tuple[dict, dict]:
+    if "BALL_INT_VALID" not in a or "BALL_INT_VALID" not in b:
+        return a, b
+    dead = (a["BALL_INT_VALID"][:, 0] == 0) & (b["BALL_INT_VALID"][:, 0] == 0)
+    if not dead.any():
+        return a, b
+    a, b = dict(a), dict(b)
+    for name in BALL_CACHE:
+        if name in a and name in b:
+            a[name], b[name] = a[name].copy(), b[name].copy()
+            a[name][dead] = 0
+            b[name][dead] = 0
+    return a, b
+
+
 def compare_snapshots(a: dict, b: dict, fields=None) -> dict:
     fields = fields or [f for f in a if f in b]
+    a, b = _mask_dead_ball_cache(a, b)
     return {name: compare_field(name, a[name], b[name]) for name in fields}
 
 
