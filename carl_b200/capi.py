@@ -150,27 +150,38 @@ class Env:
         self.n_sim, self.n_cars, self.obs_dim, self.act_dim, self.state_dim = list(dims)
         self.device = device
         self._ext_stream = None
+        self._pending: list = []
 
-    def _order_after_torch(self, *inputs) -> None:
+    def _order_after_torch(self, *inputs) -> list:
         """Orders the env stream after the producer of torch CUDA inputs.
 
         Device inputs are read on the env's own (non-blocking) stream; a torch
         tensor may still be being written on torch's current stream, so the env
         stream waits for it, as the reference's DLPack handoff
-        (``__dlpack__(stream=env_stream)``) does.  Each input is also recorded on
-        the env stream so torch's caching allocator does not hand its memory to
-        a new tensor before the env's reads of it have run."""
-        waited = False
-        for x in inputs:
-            if x is not None and getattr(x, "is_cuda", False):
-                import torch
+        (``__dlpack__(stream=env_stream)``) does.  Returns the torch inputs, which
+        `_keep_until_read` holds until the env stream has passed the call."""
+        tensors = [x for x in inputs if x is not None and getattr(x, "is_cuda", False)]
+        if tensors:
+            import torch
 
-                if self._ext_stream is None:
-                    self._ext_stream = torch.cuda.ExternalStream(self.stream, device=x.device)
-                if not waited:
-                    self._ext_stream.wait_stream(torch.cuda.current_stream(x.device))
-                    waited = True
-                x.record_stream(self._ext_stream)
+            if self._ext_stream is None:
+                self._ext_stream = torch.cuda.ExternalStream(self.stream, device=tensors[0].device)
+            self._ext_stream.wait_stream(torch.cuda.current_stream(tensors[0].device))
+        return tensors
+
+    def _keep_until_read(self, tensors: list) -> None:
+        """Keeps torch inputs alive (so torch's caching allocator cannot hand
+        their memory to new tensors) until an event recorded on the env stream
+        after the reads has completed, like the reference's pending-reset
+        capsules (python/carl.cu:613-629)."""
+        import torch
+
+        while self._pending and self._pending[0][0].query():
+            self._pending.pop(0)
+        if tensors:
+            ev = torch.cuda.Event()
+            ev.record(self._ext_stream)
+            self._pending.append((ev, tensors))
 
     def _check(self, st: int) -> None:
         if st != OK:
@@ -178,6 +189,9 @@ class Env:
 
     def close(self) -> None:
         if getattr(self, "_h", None):
+            self._lib.carlb_synchronize(self._h)
+            self._pending = []
+            self._ext_stream = None
             self._lib.carlb_destroy(self._h)
             self._h = None
 
@@ -189,15 +203,17 @@ class Env:
 
     # ---- stepping ----
     def ticks(self, kind: int, actions, n_ticks: int) -> None:
-        self._order_after_torch(actions)
+        keep = self._order_after_torch(actions)
         self._check(self._lib.carlb_ticks(self._h, kind, _ptr(actions), n_ticks))
+        self._keep_until_read(keep)
 
     def ticks_host(self, kind: int, host_actions: np.ndarray, n_ticks: int, host_rewards: np.ndarray | None = None) -> None:
         self._check(self._lib.carlb_ticks_host(self._h, kind, _ptr(host_actions), n_ticks, _ptr(host_rewards)))
 
     def env_step(self, kind: int, actions) -> None:
-        self._order_after_torch(actions)
+        keep = self._order_after_torch(actions)
         self._check(self._lib.carlb_env_step(self._h, kind, _ptr(actions)))
+        self._keep_until_read(keep)
 
     def reset(self) -> None:
         self._check(self._lib.carlb_reset(self._h))
@@ -211,28 +227,34 @@ class Env:
                           episode_ticks=None, simulation_indices=None, reset_mask=None) -> None:
         args = [ball_position, ball_velocity, ball_angular_velocity, car_position, car_rotation, car_velocity,
                 car_angular_velocity, car_demoed]
-        self._order_after_torch(*args, car_boost, car_internal_state, blue_score, simulation_indices, reset_mask)
+        keep = self._order_after_torch(*args, car_boost, car_internal_state, blue_score, orange_score,
+                                       episode_ticks, simulation_indices, reset_mask)
         self._check(self._lib.carlb_apply_reset_state(
             self._h, n_selected, *[_ptr(a) for a in args], int(demoed_is_byte), _ptr(car_boost),
             _ptr(car_internal_state), _ptr(blue_score), _ptr(orange_score), _ptr(episode_ticks),
             _ptr(simulation_indices), _ptr(reset_mask)))
+        self._keep_until_read(keep)
 
     def set_ball(self, n, pos, vel, ang, indices=None) -> None:
-        self._order_after_torch(pos, vel, ang, indices)
+        keep = self._order_after_torch(pos, vel, ang, indices)
         self._check(self._lib.carlb_set_ball(self._h, n, _ptr(pos), _ptr(vel), _ptr(ang), _ptr(indices)))
+        self._keep_until_read(keep)
 
     def set_car(self, n, pos, rot, vel, ang, demoed, demoed_is_byte, boost=None, internal=None, indices=None) -> None:
-        self._order_after_torch(pos, rot, vel, ang, demoed, boost, internal, indices)
+        keep = self._order_after_torch(pos, rot, vel, ang, demoed, boost, internal, indices)
         self._check(self._lib.carlb_set_car(self._h, n, _ptr(pos), _ptr(rot), _ptr(vel), _ptr(ang), _ptr(demoed),
                                             int(demoed_is_byte), _ptr(boost), _ptr(internal), _ptr(indices)))
+        self._keep_until_read(keep)
 
     def set_match_state(self, n, blue, orange, ticks, indices=None) -> None:
-        self._order_after_torch(blue, orange, ticks, indices)
+        keep = self._order_after_torch(blue, orange, ticks, indices)
         self._check(self._lib.carlb_set_match_state(self._h, n, _ptr(blue), _ptr(orange), _ptr(ticks), _ptr(indices)))
+        self._keep_until_read(keep)
 
     def reset_boost_pads(self, n, indices=None) -> None:
-        self._order_after_torch(indices)
+        keep = self._order_after_torch(indices)
         self._check(self._lib.carlb_reset_boost_pads(self._h, n, _ptr(indices)))
+        self._keep_until_read(keep)
 
     # ---- outputs / properties ----
     def buffer(self, which: int):
