@@ -8,6 +8,8 @@
 // entry point exits the process.
 #include <dlfcn.h>
 
+#include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <map>
@@ -76,6 +78,8 @@ struct carlb_env
 
     float4* triV = nullptr;
     float4* triAng = nullptr;
+    float4* cellSph = nullptr;
+    float carReach = 0.f;
     int* cellStart = nullptr;
     int* cellTris = nullptr;
     int hitWords = 1;
@@ -112,7 +116,7 @@ struct carlb_env
         g.simOffset = cfg.sim_offset;
         return g;
     }
-    ArenaDev arena() const { return ArenaDev{ triV, triAng, cellStart, cellTris, hitWords }; }
+    ArenaDev arena() const { return ArenaDev{ triV, triAng, cellStart, cellTris, hitWords, cellSph, carReach }; }
     Outputs outputs() const
     {
         return Outputs{ rewards, dones, scoreDiff, episodeTicks, tScoreDiff, tEpisodeTicks, overtime, tovertime };
@@ -371,6 +375,46 @@ static carlb_status initEnv(carlb_env* p, const carlb_config* cfg)
         }
         triAng[t] = make_float4(host->edgeAngles[3 * t], host->edgeAngles[3 * t + 1], host->edgeAngles[3 * t + 2], 0.f);
     }
+    // Bounding spheres for the candidate culls, stored per cell-list entry so a
+    // reject costs one load: a triangle whose sphere is farther than carReach
+    // from a car's box centre can neither overlap the box (SAT) nor meet a wheel
+    // ray, and one farther than the contact radius from the ball cannot touch
+    // it, so skipping it leaves every result unchanged.
+    std::vector<float4> triSph(nTris);
+    for (int t = 0; t < nTris; t++)
+    {
+        double c[3] = { 0, 0, 0 };
+        for (int k = 0; k < 3; k++)
+            for (int d = 0; d < 3; d++) c[d] += (double)host->verts[3 * host->tris[3 * t + k] + d] / 3.0;
+        double r2 = 0;
+        for (int k = 0; k < 3; k++)
+        {
+            double q = 0;
+            for (int d = 0; d < 3; d++)
+            {
+                const double e = (double)host->verts[3 * host->tris[3 * t + k] + d] - c[d];
+                q += e * e;
+            }
+            r2 = std::max(r2, q);
+        }
+        triSph[t] = make_float4((float)c[0], (float)c[1], (float)c[2], (float)(std::sqrt(r2) * (1.0 + 1e-6) + 1e-2));
+    }
+    {
+        double reach = std::sqrt((double)CAR_HALF_X * CAR_HALF_X + (double)CAR_HALF_Y * CAR_HALF_Y +
+                                 (double)CAR_HALF_Z * CAR_HALF_Z);
+        for (int w = 0; w < NUM_WHEELS; w++)
+        {
+            const V3 conn = suspConnection(w);
+            const double arm = std::sqrt((double)conn.x * conn.x + (double)conn.y * conn.y + (double)conn.z * conn.z);
+            reach = std::max(reach, arm + (double)suspRayLength(w) + 1.0);
+        }
+        p->carReach = (float)(reach + 2.0);  // 2 uu margin over float rounding
+    }
+    std::vector<float4> cellSph(host->cellTris.size());
+    for (size_t e = 0; e < cellSph.size(); e++) cellSph[e] = triSph[host->cellTris[e]];
+    ECHECK(p, allocZero(p, &p->cellSph, cellSph.size()));
+    ECHECK(p, cudaMemcpyAsync(p->cellSph, cellSph.data(), cellSph.size() * sizeof(float4), cudaMemcpyHostToDevice,
+                              p->stream));
     ECHECK(p, allocZero(p, &p->triV, triV.size()));
     ECHECK(p, allocZero(p, &p->triAng, triAng.size()));
     ECHECK(p, allocZero(p, &p->cellStart, host->cellStart.size()));

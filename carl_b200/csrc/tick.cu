@@ -122,10 +122,14 @@ __device__ Controls decodeAction(const void* actions, int kind, long long row)
     return c;
 }
 
-// ---- ball stage of one sim, executed by one warp ---------------------------------------
+// ---- ball stage, part 1: arena contacts of one sim, executed by one warp ------------------
+//
+// Per-sim values handed to part 2 (BallScratch words, one row per sim):
+// 0-2 the exported position at stage start, 3-5 posBT, 6-8 preSolveBT, 9-11 pushVel.
+constexpr int BALL_SCRATCH_WORDS = 12;
 
-__device__ void ballStage(const SmemSoa& cars, const SmemSoa& sims, int s, int nCars, int tick,
-                          const ArenaDev& arena, int* wbuf, int lane)
+__device__ void ballArenaStage(const SmemSoa& cars, const SmemSoa& sims, int s, int nCars, int tick,
+                               const ArenaDev& arena, int* wbuf, int lane, float* scratch, int scratchStride)
 {
     const int carBase = s * nCars;
     const V3 ballVel = sims.v(S_BVEL, s);
@@ -134,8 +138,8 @@ __device__ void ballStage(const SmemSoa& cars, const SmemSoa& sims, int s, int n
     const V3 exportedPos = sims.v(S_BPOS, s);
     const bool valid = sims.n(S_IVALID, s) != 0;
 
-    V3 posBT = valid && lensq(exportedPos - sims.v(S_EPOS, s)) == 0.f ? sims.v(S_IPOS, s) : exportedPos * .02f;
-    V3 velBT = valid && lensq(ballVel - sims.v(S_EVEL, s)) == 0.f ? sims.v(S_IVEL, s) : ballVel * .02f;
+    const V3 posBT = valid && lensq(exportedPos - sims.v(S_EPOS, s)) == 0.f ? sims.v(S_IPOS, s) : exportedPos * .02f;
+    const V3 velBT = valid && lensq(ballVel - sims.v(S_EVEL, s)) == 0.f ? sims.v(S_IVEL, s) : ballVel * .02f;
     const V3 dampedBT = sleeping ? velBT : velBT * powf(1.f - BALL_DRAG, PHYS_DT);
     const V3 preSolveBT = sleeping ? velBT : dampedBT + (V3{ 0.f, 0.f, GRAVITY_Z } * .02f) * PHYS_DT;
     const V3 velNoExt = dampedBT * 50.f;
@@ -162,6 +166,11 @@ __device__ void ballStage(const SmemSoa& cars, const SmemSoa& sims, int s, int n
             const int end = __ldg(&arena.cellStart[cell + 1]);
             for (int e = start + lane; e < end; e += 32)
             {
+                // A triangle beyond the contact radius (plus 1 uu) cannot touch the ball.
+                const float4 sph = __ldg(&arena.cellSph[e]);
+                const float dx = sph.x - center.x, dy = sph.y - center.y, dz = sph.z - center.z;
+                const float rr = sph.w + (BALL_COLLISION_RADIUS + BALL_ARENA_CONTACT_BREAK + 1.f);
+                if (dx * dx + dy * dy + dz * dz > rr * rr) continue;
                 const int tri = __ldg(&arena.cellTris[e]);
                 V3 v0, v1, v2;
                 int flags;
@@ -261,38 +270,59 @@ __device__ void ballStage(const SmemSoa& cars, const SmemSoa& sims, int s, int n
             pushVel = body.pushVel;
         }
     }
-    __syncwarp();
-
-    // Ball vs cars: distance gates across lanes (they use the pre-contact ball
-    // position), contacts in car order on lane 0.
-    bool gate = false;
-    if (lane < nCars)
-    {
-        const int i = carBase + lane;
-        gate = !cars.n(C_DEMOED, i) && ballCarGate(exportedPos, cars.v(C_CEN, i));
-    }
-    const unsigned gates = __ballot_sync(FULL, gate);
     if (lane == 0)
     {
-        for (unsigned m = gates; m; m &= m - 1)
-            solveBallCar(cars, carBase + __ffs(m) - 1, sims, s, preSolveVel, tick);
-
-        const V3 corrected = sims.v(S_BPOS, s);
-        if (lensq(corrected - exportedPos) != 0.f) posBT = corrected * .02f;
-        const V3 finalVel = sims.v(S_BVEL, s);
-        velBT = lensq(finalVel - preSolveVel) == 0.f ? preSolveBT : finalVel * .02f;
-        posBT = posBT + (pushVel * .02f) * PHYS_DT;
-        posBT = posBT + velBT * PHYS_DT;
-        const V3 ballPos = posBT * 50.f;
-        sims.setv(S_BPOS, s, ballPos);
-        sims.setv(S_IPOS, s, posBT);
-        sims.setv(S_IVEL, s, velBT);
-        sims.setv(S_EPOS, s, ballPos);
-        sims.setv(S_EVEL, s, finalVel);
-        sims.n(S_IVALID, s) = 1;
-        detectGoal(sims, s, ballPos, tick);
+        const V3 out[4] = { exportedPos, posBT, preSolveBT, pushVel };
+        #pragma unroll
+        for (int k = 0; k < 4; k++)
+        {
+            scratch[(3 * k) * scratchStride + s] = out[k].x;
+            scratch[(3 * k + 1) * scratchStride + s] = out[k].y;
+            scratch[(3 * k + 2) * scratchStride + s] = out[k].z;
+        }
     }
     __syncwarp();
+}
+
+// ---- ball stage, part 2: ball vs cars (in car order), integration, goal; one thread ----------
+__device__ void ballFinishStage(const SmemSoa& cars, const SmemSoa& sims, int s, int nCars, int tick,
+                                const float* scratch, int scratchStride)
+{
+    V3 in[4];
+    #pragma unroll
+    for (int k = 0; k < 4; k++)
+        in[k] = V3{ scratch[(3 * k) * scratchStride + s], scratch[(3 * k + 1) * scratchStride + s],
+                    scratch[(3 * k + 2) * scratchStride + s] };
+    const V3 exportedPos = in[0];
+    V3 posBT = in[1];
+    const V3 preSolveBT = in[2];
+    const V3 pushVel = in[3];
+    const V3 preSolveVel = preSolveBT * 50.f;
+
+    // Distance gates use the pre-contact ball position; a solve only moves its
+    // own car and the ball, so gating each car just before its solve is the same.
+    const int carBase = s * nCars;
+    for (int k = 0; k < nCars; k++)
+    {
+        const int i = carBase + k;
+        if (!cars.n(C_DEMOED, i) && ballCarGate(exportedPos, cars.v(C_CEN, i)))
+            solveBallCar(cars, i, sims, s, preSolveVel, tick);
+    }
+
+    const V3 corrected = sims.v(S_BPOS, s);
+    if (lensq(corrected - exportedPos) != 0.f) posBT = corrected * .02f;
+    const V3 finalVel = sims.v(S_BVEL, s);
+    const V3 velBT = lensq(finalVel - preSolveVel) == 0.f ? preSolveBT : finalVel * .02f;
+    posBT = posBT + (pushVel * .02f) * PHYS_DT;
+    posBT = posBT + velBT * PHYS_DT;
+    const V3 ballPos = posBT * 50.f;
+    sims.setv(S_BPOS, s, ballPos);
+    sims.setv(S_IPOS, s, posBT);
+    sims.setv(S_IVEL, s, velBT);
+    sims.setv(S_EPOS, s, ballPos);
+    sims.setv(S_EVEL, s, finalVel);
+    sims.n(S_IVALID, s) = 1;
+    detectGoal(sims, s, ballPos, tick);
 }
 
 // ---- the kernel -------------------------------------------------------------------------
@@ -351,8 +381,10 @@ __global__ void __launch_bounds__(256) tickKernel(TickParams p, ArenaDev arena)
             const V3 cen = cars.v(C_CEN, tid);
             const Q4 rot = cars.q(C_ROT, tid);
             const int cell = broadphaseCell(pos, vel, ang, cen, rot);
-            cellS[tid] = cell;
-            cntS[tid] = __ldg(&arena.cellStart[cell + 1]) - __ldg(&arena.cellStart[cell]);
+            const int first = __ldg(&arena.cellStart[cell]);
+            cellS[tid] = first;  // first entry of the car's candidate list
+            cntS[tid] = __ldg(&arena.cellStart[cell + 1]) - first;
+            if (lastTick && p.diagCar) p.diagCar[0 * p.carStride + carBase + tid] = cell;
             const V3 up = rotate(rot, axisVec(2));
             #pragma unroll
             for (int w = 0; w < NUM_WHEELS; w++)
@@ -405,6 +437,12 @@ __global__ void __launch_bounds__(256) tickKernel(TickParams p, ArenaDev arena)
 
         // ---- flattened (car, candidate) work: wheel rays and SAT ----
         const int total = preS[carsHere];
+        if (tid == 0)
+        {
+            // Solve-order counters for the next stage (the scan's sums are dead now).
+            wsumS[1] = 0;
+            wsumS[2] = 0;
+        }
         for (int it = tid; it < total; it += blockDim.x)
         {
             int lo = 0, hi = carsHere - 1;
@@ -416,7 +454,17 @@ __global__ void __launch_bounds__(256) tickKernel(TickParams p, ArenaDev arena)
             }
             const int c = lo;
             const int k = it - preS[c];
-            const int tri = __ldg(&arena.cellTris[__ldg(&arena.cellStart[cellS[c]]) + k]);
+            const int e = cellS[c] + k;
+            {
+                // Triangles out of reach of the box and the wheel rays cannot
+                // produce a ray hit or a SAT overlap.
+                const float4 sph = __ldg(&arena.cellSph[e]);
+                const V3 cc = cars.v(C_CEN, c);
+                const float dx = sph.x - cc.x, dy = sph.y - cc.y, dz = sph.z - cc.z;
+                const float rr = sph.w + arena.carReach;
+                if (dx * dx + dy * dy + dz * dz > rr * rr) continue;
+            }
+            const int tri = __ldg(&arena.cellTris[e]);
             V3 v0, v1, v2;
             int flags;
             loadTri(arena, tri, v0, v1, v2, flags);
@@ -467,7 +515,7 @@ __global__ void __launch_bounds__(256) tickKernel(TickParams p, ArenaDev arena)
             const V3 dir = neg(up);
             int src[NUM_WHEELS];
             V3 start[NUM_WHEELS];
-            const int cellFirst = __ldg(&arena.cellStart[cellS[i]]);
+            const int cellFirst = cellS[i];
             #pragma unroll
             for (int w = 0; w < NUM_WHEELS; w++)
             {
@@ -590,22 +638,53 @@ __global__ void __launch_bounds__(256) tickKernel(TickParams p, ArenaDev arena)
             cars.setv(C_ANG, i, ang);
             storeInternal(cars, i, s);
             storeSusp(cars, i, su);
+
+            // Hand the ray results to whichever thread solves this car: the
+            // distances go into the car's own (already consumed) ray keys, the
+            // normals over its own ray starts.
+            float* rd = reinterpret_cast<float*>(keyS) + 8 * i;
+            #pragma unroll
+            for (int w = 0; w < NUM_WHEELS; w++)
+            {
+                rd[w] = rayDist[w];
+                rsS[(3 * w) * L.TC + i] = rayNormal[w].x;
+                rsS[(3 * w + 1) * L.TC + i] = rayNormal[w].y;
+                rsS[(3 * w + 2) * L.TC + i] = rayNormal[w].z;
+            }
+            // Solve order: cars likely to have mesh or plane contacts first, so the
+            // long contact path runs in as few warps as possible.
+            bool heavy = false;
+            if (!cars.n(C_DEMOED, i))
+            {
+                heavy = cars.n(C_MAN_COUNT, i) > 0;
+                for (int h = 0; h < L.HW && !heavy; h++) heavy = hitS[h * L.TC + i] != 0u;
+            }
+            const int slot = heavy ? atomicAdd(&wsumS[1], 1) : carsHere - 1 - atomicAdd(&wsumS[2], 1);
+            preS[slot] = i;
         }
         __syncthreads();  // every ray has read the other cars' poses
 
-        // ---- per car: SAT contacts, suspension, manifold, solve ----
+        // ---- per car (in solve order): SAT contacts, suspension, manifold, solve ----
         if (carThread)
         {
-            const int i = tid;
+            const int i = preS[tid];
+            {
+                const float* rd = reinterpret_cast<const float*>(keyS) + 8 * i;
+                #pragma unroll
+                for (int w = 0; w < NUM_WHEELS; w++)
+                {
+                    rayDist[w] = rd[w];
+                    rayNormal[w] = V3{ rsS[(3 * w) * L.TC + i], rsS[(3 * w + 1) * L.TC + i], rsS[(3 * w + 2) * L.TC + i] };
+                }
+            }
             const V3 cen = cars.v(C_CEN, i);
             const Q4 rot = cars.q(C_ROT, i);
-            const int cellFirst = __ldg(&arena.cellStart[cellS[i]]);
+            const int cellFirst = cellS[i];
             const int nCand = cntS[i];
 
             if (lastTick && p.diagCar)
             {
                 const long long g = carBase + i;
-                p.diagCar[0 * p.carStride + g] = cellS[i];
                 p.diagCar[1 * p.carStride + g] = nCand;
                 int nh = 0;
                 for (int h = 0; h < L.HW && nh < MAX_CAR_TRI_PAIRS; h++)
@@ -694,34 +773,31 @@ __global__ void __launch_bounds__(256) tickKernel(TickParams p, ArenaDev arena)
                 }
             }
         }
+        if (tid == 0) wsumS[0] = 0;  // car-car work counter (the scan's sums are dead here)
         __syncthreads();
 
-        // ---- per sim (one warp each): car-car pairs, then the ball ----
-        for (int s = warp; s < simsHere; s += L.W)
+        // ---- car-car pairs: one thread per sim that has a pair within reach ----
+        // Sims are independent, so the compacted order does not affect results;
+        // within a sim the pairs run in the reference's order (a < b).
         {
-            const int sb = s * nCars;
+            int* activeS = cntS;  // per-car counts are dead until the next tick
+            int& nActive = wsumS[0];
             const int nPairs = nCars * (nCars - 1) / 2;
-            bool gate = false;
-            int pa = 0, pb = 0;
-            if (lane < nPairs)
+            if (tid < simsHere)
             {
-                int q = lane;
-                for (int a = 0; a < nCars - 1; a++)
-                {
-                    const int span = nCars - 1 - a;
-                    if (q < span)
-                    {
-                        pa = a;
-                        pb = a + 1 + q;
-                        break;
-                    }
-                    q -= span;
-                }
-                gate = carCarGate(cars, sb + pb, sb + pa);
+                const int sb = tid * nCars;
+                bool gate = false;
+                for (int a = 0; a < nCars - 1 && !gate; a++)
+                    for (int b = a + 1; b < nCars && !gate; b++) gate = carCarGate(cars, sb + b, sb + a);
+                if (gate) activeS[atomicAdd(&nActive, 1)] = tid;
+                else if (lastTick && p.diagSim)
+                    for (int q = 0; q < nPairs && q < DIAG_SIM_WORDS; q++) p.diagSim[q * p.simStride + simBase + tid] = 0;
             }
-            const unsigned anyGate = __ballot_sync(FULL, gate);
-            if (anyGate && lane == 0)
+            __syncthreads();
+            for (int j = tid; j < nActive; j += blockDim.x)
             {
+                const int sIdx = activeS[j];
+                const int sb = sIdx * nCars;
                 SimCars<SmemSoa> sc{ cars, sb, nCars, p.nBlue, (int)(p.globalCarBase + carBase + sb), tick, p.seed };
                 int pair = 0;
                 for (int a = 0; a < nCars - 1; a++)
@@ -729,16 +805,17 @@ __global__ void __launch_bounds__(256) tickKernel(TickParams p, ArenaDev arena)
                     {
                         const int kept = solveCarCarPair(sc, b, a);
                         if (lastTick && p.diagSim && pair < DIAG_SIM_WORDS)
-                            p.diagSim[pair * p.simStride + simBase + s] = kept;
+                            p.diagSim[pair * p.simStride + simBase + sIdx] = kept;
                     }
             }
-            else if (!anyGate && lastTick && p.diagSim && lane < nPairs && lane < DIAG_SIM_WORDS)
-            {
-                p.diagSim[lane * p.simStride + simBase + s] = 0;
-            }
-            __syncwarp();
-            ballStage(cars, sims, s, nCars, tick, arena, wbuf, lane);
         }
+        __syncthreads();
+
+        // ---- ball: arena contacts (one warp per sim), then cars + integration (one thread per sim) ----
+        for (int s = warp; s < simsHere; s += L.W)
+            ballArenaStage(cars, sims, s, nCars, tick, arena, wbuf, lane, rsS, L.TS);
+        __syncthreads();
+        if (tid < simsHere) ballFinishStage(cars, sims, tid, nCars, tick, rsS, L.TS);
         __syncthreads();
 
         // ---- per car: integrate, finish tick; per sim: finish ball ----
@@ -763,10 +840,14 @@ __global__ void __launch_bounds__(256) tickKernel(TickParams p, ArenaDev arena)
         __syncthreads();
 
         // ---- boost pads ----
+        // Pad-major item order: a warp's lanes share a pad, so the pad table
+        // reads from constant memory are warp-uniform.  Pads never overlap, so
+        // no car can be claimed by two pads in the same tick.
         for (int it = tid; it < simsHere * NUM_BOOST_PADS; it += blockDim.x)
         {
-            const int s = it / NUM_BOOST_PADS;
-            boostPad(cars, s * nCars, nCars, sims, s, it - s * NUM_BOOST_PADS, c_tables);
+            const int pad = it / simsHere;
+            const int s = it - pad * simsHere;
+            boostPad(cars, s * nCars, nCars, sims, s, pad, c_tables);
         }
         __syncthreads();
 

@@ -17,6 +17,9 @@ struct ArenaDev
     const int* cellStart;   // [NUM_CELLS + 1]
     const int* cellTris;    // [cellStart[NUM_CELLS]]
     int hitWords;           // ceil(max triangles per cell / 32)
+    const float4* cellSph;  // [cellStart[NUM_CELLS]]: bounding sphere of cellTris[e] (centre xyz, radius w),
+                            // radius rounded up
+    float carReach;         // radius around a car's box centre that holds its box and wheel rays, plus margin
 };
 
 struct TickParams
