@@ -84,6 +84,11 @@ struct carlb_env
     int* cellTris = nullptr;
     int hitWords = 1;
 
+    // Tick path: the staged kernel sequence with its scratch (default), or the
+    // fused per-tile kernel (CARLB_TICK_PATH=fused, read at create).
+    bool staged = true;
+    StageScratch scratch{};
+
     float *obs = nullptr, *tobs = nullptr, *packed = nullptr, *tpacked = nullptr, *rewards = nullptr;
     uint8_t *dones = nullptr, *overtime = nullptr, *tovertime = nullptr;
     int *scoreDiff = nullptr, *episodeTicks = nullptr, *tScoreDiff = nullptr, *tEpisodeTicks = nullptr;
@@ -191,7 +196,8 @@ carlb_status launchTicks(carlb_env* e, carlb_action_kind kind, int nTicks)
     p.tileSims = e->tileSims;
     p.compatFlags = e->cfg.compat_flags;
     ECHECK(e, cudaEventRecord(e->ev0, e->stream));
-    const int err = launchTick(p, e->arena(), e->stream);
+    const int err = e->staged ? launchTickStaged(p, e->arena(), e->scratch, e->stream)
+                              : launchTick(p, e->arena(), e->stream);
     if (err) return cudaFail(e, (cudaError_t)err, "tick kernel launch");
     ECHECK(e, cudaEventRecord(e->ev1, e->stream));
     e->tick += nTicks;
@@ -354,6 +360,19 @@ static carlb_status initEnv(carlb_env* p, const carlb_config* cfg)
     ECHECK(p, allocZero(p, &p->episodeTicks, (size_t)cfg->n_sim));
     ECHECK(p, allocZero(p, &p->tScoreDiff, (size_t)cfg->n_sim));
     ECHECK(p, allocZero(p, &p->tEpisodeTicks, (size_t)cfg->n_sim));
+    {
+        const char* path = std::getenv("CARLB_TICK_PATH");
+        p->staged = !(path && std::string(path) == "fused");
+    }
+    if (p->staged)
+    {
+        ECHECK(p, allocZero(p, &p->scratch.first, (size_t)p->carStride));
+        ECHECK(p, allocZero(p, &p->scratch.cnt, (size_t)p->carStride));
+        ECHECK(p, allocZero(p, &p->scratch.ray, (size_t)16 * p->carStride));
+        ECHECK(p, allocZero(p, &p->scratch.hits, (size_t)p->hitWords * p->carStride));
+        ECHECK(p, allocZero(p, &p->scratch.wheelBits, (size_t)p->carStride));
+        ECHECK(p, allocZero(p, &p->scratch.ball, (size_t)12 * p->simStride));
+    }
     p->actionCapacity = (size_t)p->nCarTotal * 32;
     {
         uint8_t* a = nullptr;

@@ -884,6 +884,559 @@ __global__ void __launch_bounds__(256) tickKernel(TickParams p, ArenaDev arena)
             p.sim[(long long)w * p.simStride + simBase + i] = sims.f(w, i);
 }
 
+
+// =========================================================================================
+// Staged path: the same tick as a sequence of kernels over the state in global memory
+// (resident in L2 between stages), so each stage runs at its own occupancy and no warp
+// waits on a CTA barrier for unrelated work.  Per tick:
+//   candKernel     begin step, broadphase, (car, candidate) rays + SAT, ray finish, controls
+//   solveKernel    suspension, plane + mesh manifold, car-arena solve
+//   carCarKernel   car-car pairs, one thread per sim with a pair in reach
+//   ballKernel     ball arena contacts, one warp per sim
+//   finishKernel   ball vs cars + integration + goal, car integration + finish, boost pads
+// =========================================================================================
+
+constexpr int CAND_BLOCK = 128;   // cars per candKernel CTA
+constexpr int SOLVE_BLOCK = 128;  // cars per solveKernel CTA
+constexpr int CC_BLOCK = 128;     // sims per carCarKernel CTA
+constexpr int BALL_WARPS = 4;     // sims (warps) per ballKernel CTA
+constexpr int FIN_THREADS = 256;  // threads per finishKernel CTA
+
+using CarSoa = Soa<int>;  // int indexing: NCW * carStride < 2^31 is checked at launch
+
+__global__ void __launch_bounds__(CAND_BLOCK) candKernel(TickParams p, ArenaDev arena, StageScratch x, int t)
+{
+    extern __shared__ __align__(16) float sm[];
+    const int B = CAND_BLOCK, HW = arena.hitWords;
+    int* cntS = reinterpret_cast<int*>(sm);                 // [B]
+    int* firstS = cntS + B;                                  // [B]
+    int* preS = firstS + B;                                  // [B + 1]
+    int* wsumS = preS + B + 1;                               // [32]
+    float* rsS = reinterpret_cast<float*>(wsumS + 32);       // [15][B] ray starts (12), dir (3)
+    float* poseS = rsS + 15 * B;                             // [7][B] cen (3), rot (4)
+    unsigned* hitS = reinterpret_cast<unsigned*>(poseS + 7 * B);  // [HW][B]
+    const size_t keyOff = ((size_t)(hitS + HW * B) - (size_t)sm + 7) & ~(size_t)7;
+    unsigned long long* keyS = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(sm) + keyOff);  // [4][B]
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int n = p.nSim * p.nCars;
+    const int first = blockIdx.x * B;
+    const int here = min(B, n - first);
+    const int i = first + tid;
+    const bool valid = tid < here;
+    const CarSoa cars{ p.car, (int)p.carStride };
+    const CarSoa sims{ p.sim, (int)p.simStride };
+    const int tick = p.tick0 + t + 1;
+    const bool lastTick = t == p.nTicks - 1;
+
+    V3 cen = v3zero(), up = v3zero();
+    Q4 rot = Q4{ 0.f, 0.f, 0.f, 1.f };
+    if (valid)
+    {
+        if (i % p.nCars == 0) sims.n(S_EP_TICKS, i / p.nCars) += 1;
+        const V3 pos = cars.v(C_POS, i), vel = cars.v(C_VEL, i), ang = cars.v(C_ANG, i);
+        cen = cars.v(C_CEN, i);
+        rot = cars.q(C_ROT, i);
+        const int cell = broadphaseCell(pos, vel, ang, cen, rot);
+        const int f0 = __ldg(&arena.cellStart[cell]);
+        firstS[tid] = f0;
+        cntS[tid] = __ldg(&arena.cellStart[cell + 1]) - f0;
+        if (lastTick && p.diagCar) p.diagCar[0 * p.carStride + i] = cell;
+        up = rotate(rot, axisVec(2));
+        #pragma unroll
+        for (int w = 0; w < NUM_WHEELS; w++)
+        {
+            const V3 st = cen + rotate(rot, suspConnection(w));
+            rsS[(3 * w) * B + tid] = st.x;
+            rsS[(3 * w + 1) * B + tid] = st.y;
+            rsS[(3 * w + 2) * B + tid] = st.z;
+            keyS[w * B + tid] = rayKey(rayLen(w) + 1.f, 0xffffffffu);
+        }
+        const V3 dir = neg(up);
+        rsS[12 * B + tid] = dir.x;
+        rsS[13 * B + tid] = dir.y;
+        rsS[14 * B + tid] = dir.z;
+        poseS[0 * B + tid] = cen.x;
+        poseS[1 * B + tid] = cen.y;
+        poseS[2 * B + tid] = cen.z;
+        poseS[3 * B + tid] = rot.x;
+        poseS[4 * B + tid] = rot.y;
+        poseS[5 * B + tid] = rot.z;
+        poseS[6 * B + tid] = rot.w;
+        for (int h = 0; h < HW; h++) hitS[h * B + tid] = 0u;
+    }
+    else
+    {
+        cntS[tid] = 0;
+    }
+
+    // Block exclusive scan of candidate counts.
+    {
+        int v = cntS[tid];
+        #pragma unroll
+        for (int d = 1; d < 32; d <<= 1)
+        {
+            const int u = __shfl_up_sync(FULL, v, d);
+            if (lane >= d) v += u;
+        }
+        if (lane == 31) wsumS[warp] = v;
+        __syncthreads();
+        if (warp == 0)
+        {
+            int q = lane < B / 32 ? wsumS[lane] : 0;
+            #pragma unroll
+            for (int d = 1; d < 32; d <<= 1)
+            {
+                const int u = __shfl_up_sync(FULL, q, d);
+                if (lane >= d) q += u;
+            }
+            if (lane < B / 32) wsumS[lane] = q;
+        }
+        __syncthreads();
+        if (warp > 0) v += wsumS[warp - 1];
+        preS[tid + 1] = v;
+        if (tid == 0) preS[0] = 0;
+    }
+    __syncthreads();
+
+    // Flattened (car, candidate) work: wheel rays and SAT.
+    const int total = preS[here];
+    for (int it = tid; it < total; it += B)
+    {
+        int lo = 0, hi = here - 1;
+        while (lo < hi)
+        {
+            const int mid = (lo + hi + 1) >> 1;
+            if (preS[mid] <= it) lo = mid;
+            else hi = mid - 1;
+        }
+        const int c = lo;
+        const int k = it - preS[c];
+        const int e = firstS[c] + k;
+        const V3 cc = { poseS[0 * B + c], poseS[1 * B + c], poseS[2 * B + c] };
+        {
+            const float4 sph = __ldg(&arena.cellSph[e]);
+            const float dx = sph.x - cc.x, dy = sph.y - cc.y, dz = sph.z - cc.z;
+            const float rr = sph.w + arena.carReach;
+            if (dx * dx + dy * dy + dz * dz > rr * rr) continue;
+        }
+        const int tri = __ldg(&arena.cellTris[e]);
+        V3 v0, v1, v2;
+        int flags;
+        loadTri(arena, tri, v0, v1, v2, flags);
+
+        const V3 dir = { rsS[12 * B + c], rsS[13 * B + c], rsS[14 * B + c] };
+        const V3 e1 = v1 - v0;
+        const V3 e2 = v2 - v0;
+        const V3 pv = cross(dir, e2);
+        const float det = dot(e1, pv);
+        if (!(fabsf(det) < RAY_PARALLEL_EPS))
+        {
+            const float invDet = 1.f / det;
+            #pragma unroll
+            for (int w = 0; w < NUM_WHEELS; w++)
+            {
+                const V3 st = { rsS[(3 * w) * B + c], rsS[(3 * w + 1) * B + c], rsS[(3 * w + 2) * B + c] };
+                const V3 tv = st - v0;
+                const float u = invDet * dot(tv, pv);
+                if (u < 0.f || u > 1.f) continue;
+                const V3 qv = cross(tv, e1);
+                const float v = invDet * dot(dir, qv);
+                if (v < 0.f || u + v > 1.f) continue;
+                const float dist = invDet * dot(e2, qv);
+                if (dist <= 0.f || !(dist < rayLen(w) + 1.f)) continue;
+                atomicMin(&keyS[w * B + c], rayKey(dist, (unsigned)k));
+            }
+        }
+        if (!(flags & 1))
+        {
+            const Q4 cr = { poseS[3 * B + c], poseS[4 * B + c], poseS[5 * B + c], poseS[6 * B + c] };
+            const LocalTri lt = localTriangle(cc, cr, v0, v1, v2);
+            if (carTriSat(lt).overlap) atomicOr(&hitS[(k >> 5) * B + c], 1u << (k & 31));
+        }
+    }
+    __syncthreads();
+    if (!valid) return;
+
+    // Finish the wheel rays: arena hit, other cars' boxes (in car order), ball.
+    const V3 dir = neg(up);
+    float rayDist[NUM_WHEELS];
+    V3 rayNormal[NUM_WHEELS];
+    int src[NUM_WHEELS];
+    V3 start[NUM_WHEELS];
+    const int cellFirst = firstS[tid];
+    #pragma unroll
+    for (int w = 0; w < NUM_WHEELS; w++)
+    {
+        start[w] = V3{ rsS[(3 * w) * B + tid], rsS[(3 * w + 1) * B + tid], rsS[(3 * w + 2) * B + tid] };
+        const unsigned long long key = keyS[w * B + tid];
+        const unsigned cand = (unsigned)(key & 0xffffffffu);
+        if (cand != 0xffffffffu)
+        {
+            rayDist[w] = __uint_as_float((unsigned)(key >> 32));
+            V3 v0, v1, v2;
+            int flags;
+            loadTri(arena, __ldg(&arena.cellTris[cellFirst + (int)cand]), v0, v1, v2, flags);
+            V3 nrm = cross(v1 - v0, v2 - v0);
+            const float nl = lensq(nrm);
+            nrm = nrm * rsqrtf(nl);
+            if (dot(nrm, dir) > 0.f) nrm = neg(nrm);
+            rayNormal[w] = nrm;
+            src[w] = WHEEL_ARENA;
+        }
+        else
+        {
+            rayDist[w] = rayLen(w) + 1.f;
+            rayNormal[w] = up;
+            src[w] = WHEEL_NONE;
+        }
+    }
+    const int mySim = i / p.nCars;
+    const int sb = mySim * p.nCars;
+    for (int k = 0; k < p.nCars; k++)
+    {
+        const int o = sb + k;
+        if (o == i || cars.n(C_DEMOED, o)) continue;
+        const V3 oc = cars.v(C_CEN, o);
+        if (lensq(oc - cen) > 250.f * 250.f) continue;  // beyond any wheel ray + box reach
+        const Q4 orot = cars.q(C_ROT, o);
+        #pragma unroll
+        for (int w = 0; w < NUM_WHEELS; w++)
+        {
+            const V3 ls = unrotate(orot, start[w] - oc);
+            const V3 ld = unrotate(orot, dir);
+            float entry = 0.f, exitD = rayLen(w);
+            int hitAxis = -1;
+            bool miss = false;
+            #pragma unroll
+            for (int a = 0; a < 3; a++)
+            {
+                const float h = vget(carHalfExtents(), a);
+                const float d = vget(ld, a), s0 = vget(ls, a);
+                if (fabsf(d) < RAY_PARALLEL_EPS)
+                {
+                    if (fabsf(s0) > h) { miss = true; break; }
+                    continue;
+                }
+                const float inv = 1.f / d;
+                const float t1 = (-h - s0) * inv;
+                const float t2 = (h - s0) * inv;
+                const float tn = fminf(t1, t2);
+                if (tn > entry)
+                {
+                    entry = tn;
+                    hitAxis = a;
+                }
+                exitD = fminf(exitD, fmaxf(t1, t2));
+                if (entry > exitD) { miss = true; break; }
+            }
+            if (miss || hitAxis < 0 || entry >= rayDist[w]) continue;
+            V3 ln = v3zero();
+            vset(ln, hitAxis, vget(ld, hitAxis) > 0.f ? -1.f : 1.f);
+            rayDist[w] = entry;
+            rayNormal[w] = rotate(orot, ln);
+            src[w] = WHEEL_CAR;
+        }
+    }
+    {
+        const V3 bp = sims.v(S_BPOS, mySim);
+        const float invR = 1.f / BALL_COLLISION_RADIUS;
+        #pragma unroll
+        for (int w = 0; w < NUM_WHEELS; w++)
+        {
+            const V3 off = start[w] - bp;
+            const float b = dot(off, dir);
+            const float cq = lensq(off) - BALL_COLLISION_RADIUS * BALL_COLLISION_RADIUS;
+            if (cq < 0.f) continue;
+            const float disc = b * b - cq;
+            if (disc < 0.f) continue;
+            const float dist = -b - sqrtf(disc);
+            if (!(dist > 0.f && dist <= rayLen(w))) continue;
+            if (dist >= rayDist[w]) continue;
+            rayDist[w] = dist;
+            rayNormal[w] = (start[w] + dir * dist - bp) * invR;
+            src[w] = WHEEL_BALL;
+        }
+    }
+    unsigned wheelBits = 0;
+    #pragma unroll
+    for (int w = 0; w < NUM_WHEELS; w++)
+        if (src[w] != WHEEL_NONE && rayDist[w] <= rayLen(w)) wheelBits |= 1u << w;
+    x.wheelBits[i] = wheelBits;
+    x.first[i] = cellFirst;
+    x.cnt[i] = cntS[tid];
+    for (int h = 0; h < HW; h++) x.hits[(long long)h * p.carStride + i] = hitS[h * B + tid];
+    #pragma unroll
+    for (int w = 0; w < NUM_WHEELS; w++)
+    {
+        x.ray[(long long)w * p.carStride + i] = rayDist[w];
+        x.ray[(long long)(4 + 3 * w) * p.carStride + i] = rayNormal[w].x;
+        x.ray[(long long)(5 + 3 * w) * p.carStride + i] = rayNormal[w].y;
+        x.ray[(long long)(6 + 3 * w) * p.carStride + i] = rayNormal[w].z;
+    }
+    if (lastTick)
+    {
+        #pragma unroll
+        for (int w = 0; w < NUM_WHEELS; w++)
+        {
+            p.carOut[(long long)(O_RAY_DIST + w) * p.carStride + i] = rayDist[w];
+            p.carOut[(long long)(O_RAY_NORMAL + 3 * w) * p.carStride + i] = rayNormal[w].x;
+            p.carOut[(long long)(O_RAY_NORMAL + 3 * w + 1) * p.carStride + i] = rayNormal[w].y;
+            p.carOut[(long long)(O_RAY_NORMAL + 3 * w + 2) * p.carStride + i] = rayNormal[w].z;
+            reinterpret_cast<int*>(p.carOut)[(long long)(O_WHEEL_SRC + w) * p.carStride + i] = src[w];
+        }
+    }
+
+    // Controls.
+    const Controls ctl = decodeAction(p.actions, p.actionKind, i);
+    V3 vel = cars.v(C_VEL, i), ang = cars.v(C_ANG, i);
+    Internal st = loadInternal(cars, i);
+    Susp su = loadSusp(cars, i);
+    processControls(ctl, cars.n(C_DEMOED, i) != 0, rot, vel, ang, st, su, rayDist, cars.n(C_MAN_COUNT, i),
+                    cars.v(C_MAN_N0, i));
+    cars.setv(C_VEL, i, vel);
+    cars.setv(C_ANG, i, ang);
+    storeInternal(cars, i, st);
+    storeSusp(cars, i, su);
+}
+
+__global__ void __launch_bounds__(SOLVE_BLOCK) solveKernel(TickParams p, ArenaDev arena, StageScratch x, int t)
+{
+    __shared__ int orderS[SOLVE_BLOCK];
+    __shared__ int countS[2];
+    const int tid = threadIdx.x;
+    const int n = p.nSim * p.nCars;
+    const int first = blockIdx.x * SOLVE_BLOCK;
+    const int here = min(SOLVE_BLOCK, n - first);
+    const CarSoa cars{ p.car, (int)p.carStride };
+    const int tick = p.tick0 + t + 1;
+    const bool lastTick = t == p.nTicks - 1;
+    const int HW = arena.hitWords;
+
+    // Cars likely to have mesh or plane contacts first, so the long contact path
+    // runs in as few warps as possible (cars are independent in this stage).
+    if (tid < 2) countS[tid] = 0;
+    __syncthreads();
+    if (tid < here)
+    {
+        const int i = first + tid;
+        bool heavy = false;
+        if (!cars.n(C_DEMOED, i))
+        {
+            heavy = cars.n(C_MAN_COUNT, i) > 0;
+            for (int h = 0; h < HW && !heavy; h++) heavy = x.hits[(long long)h * p.carStride + i] != 0u;
+        }
+        const int slot = heavy ? atomicAdd(&countS[0], 1) : here - 1 - atomicAdd(&countS[1], 1);
+        orderS[slot] = i;
+    }
+    __syncthreads();
+    if (tid >= here) return;
+    const int i = orderS[tid];
+
+    const V3 cen = cars.v(C_CEN, i);
+    const Q4 rot = cars.q(C_ROT, i);
+    const int cellFirst = x.first[i];
+    if (lastTick && p.diagCar)
+    {
+        p.diagCar[1 * p.carStride + i] = x.cnt[i];
+        int nh = 0;
+        for (int h = 0; h < HW && nh < MAX_CAR_TRI_PAIRS; h++)
+            for (unsigned m = x.hits[(long long)h * p.carStride + i]; m && nh < MAX_CAR_TRI_PAIRS; m &= m - 1)
+            {
+                const int k = h * 32 + __ffs(m) - 1;
+                p.diagCar[(3 + nh) * p.carStride + i] = __ldg(&arena.cellTris[cellFirst + k]);
+                nh++;
+            }
+        p.diagCar[2 * p.carStride + i] = nh;
+        for (int r = nh; r < MAX_CAR_TRI_PAIRS; r++) p.diagCar[(3 + r) * p.carStride + i] = -1;
+    }
+    if (cars.n(C_DEMOED, i)) return;
+
+    float rayDist[NUM_WHEELS];
+    V3 rayNormal[NUM_WHEELS];
+    #pragma unroll
+    for (int w = 0; w < NUM_WHEELS; w++)
+    {
+        rayDist[w] = x.ray[(long long)w * p.carStride + i];
+        rayNormal[w] = V3{ x.ray[(long long)(4 + 3 * w) * p.carStride + i], x.ray[(long long)(5 + 3 * w) * p.carStride + i],
+                           x.ray[(long long)(6 + 3 * w) * p.carStride + i] };
+    }
+    Body body = loadCarBody(cars, i);
+    Susp su = loadSusp(cars, i);
+    float lat[NUM_WHEELS], lon[NUM_WHEELS];
+    #pragma unroll
+    for (int w = 0; w < NUM_WHEELS; w++)
+    {
+        lat[w] = cars.f(C_LAT + w, i);
+        lon[w] = cars.f(C_LON + w, i);
+    }
+    applySuspension(body, su, lat, lon, rayDist, rayNormal, cars.n(C_MAN_COUNT, i), cars.v(C_MAN_N0, i), tick,
+                    (p.compatFlags & 1) != 0);
+
+    MPoint pts[MAX_CAR_MANIFOLD_POINTS];
+    int count = planeManifold(cen, rot, pts);
+    const int planeCount = count;
+    Contact best{};
+    float bestDist = 3.402823466e+38f;
+    int bestTri = -1;
+    int seen = 0;
+    for (int h = 0; h < HW && seen < MAX_CAR_TRI_PAIRS; h++)
+    {
+        for (unsigned m = x.hits[(long long)h * p.carStride + i]; m && seen < MAX_CAR_TRI_PAIRS; m &= m - 1)
+        {
+            seen++;
+            const int k = h * 32 + __ffs(m) - 1;
+            const int tri = __ldg(&arena.cellTris[cellFirst + k]);
+            V3 v0, v1, v2;
+            int flags;
+            loadTri(arena, tri, v0, v1, v2, flags);
+            const LocalTri lt = localTriangle(cen, rot, v0, v1, v2);
+            const Sat sat = carTriSat(lt);
+            pairContacts(lt, sat, [&](const Contact& c) {
+                if (nearManifoldPoint(pts, planeCount, c.carPos)) return;
+                const float d = -c.depth;
+                if (d < bestDist)
+                {
+                    bestDist = d;
+                    best = c;
+                    bestTri = tri;
+                }
+            });
+        }
+    }
+    if (bestTri >= 0)
+    {
+        V3 v0, v1, v2;
+        int flags;
+        loadTri(arena, bestTri, v0, v1, v2, flags);
+        adjustInternalEdge(localTriangle(cen, rot, v0, v1, v2), triAngles(arena, bestTri), best);
+        addManifoldPoint(pts, count, contactToManifold(best, cen, rot));
+    }
+    if (count > 0)
+    {
+        solveCarManifold(body, pts, count);
+        integrateSplitCorrection(body);
+    }
+    cars.n(C_MAN_COUNT, i) = count;
+    cars.setv(C_MAN_N0, i, count > 0 ? pts[0].worldNormal : v3zero());
+    body.vel = body.vel + body.extVel + body.deltaVel;
+    body.ang = body.ang + body.extAng + body.deltaAng;
+    storeCarBody(cars, i, body);
+    storeSusp(cars, i, su);
+    #pragma unroll
+    for (int w = 0; w < NUM_WHEELS; w++)
+    {
+        cars.f(C_LAT + w, i) = lat[w];
+        cars.f(C_LON + w, i) = lon[w];
+    }
+}
+
+__global__ void __launch_bounds__(CC_BLOCK) carCarKernel(TickParams p, int t)
+{
+    __shared__ int activeS[CC_BLOCK];
+    __shared__ int nActive;
+    const int tid = threadIdx.x;
+    const int s = blockIdx.x * CC_BLOCK + tid;
+    const CarSoa cars{ p.car, (int)p.carStride };
+    const int nCars = p.nCars;
+    const int tick = p.tick0 + t + 1;
+    const bool lastTick = t == p.nTicks - 1;
+    const int nPairs = nCars * (nCars - 1) / 2;
+    if (tid == 0) nActive = 0;
+    __syncthreads();
+    if (s < p.nSim)
+    {
+        const int sb = s * nCars;
+        bool gate = false;
+        for (int a = 0; a < nCars - 1 && !gate; a++)
+            for (int b = a + 1; b < nCars && !gate; b++) gate = carCarGate(cars, sb + b, sb + a);
+        if (gate) activeS[atomicAdd(&nActive, 1)] = s;
+        else if (lastTick && p.diagSim)
+            for (int q = 0; q < nPairs && q < DIAG_SIM_WORDS; q++) p.diagSim[q * p.simStride + s] = 0;
+    }
+    __syncthreads();
+    if (tid >= nActive) return;
+    const int sIdx = activeS[tid];
+    const int sb = sIdx * nCars;
+    SimCars<CarSoa> sc{ cars, sb, nCars, p.nBlue, (int)(p.globalCarBase + sb), tick, p.seed };
+    int pair = 0;
+    for (int a = 0; a < nCars - 1; a++)
+        for (int b = a + 1; b < nCars; b++, pair++)
+        {
+            const int kept = solveCarCarPair(sc, b, a);
+            if (lastTick && p.diagSim && pair < DIAG_SIM_WORDS) p.diagSim[pair * p.simStride + sIdx] = kept;
+        }
+}
+
+__global__ void __launch_bounds__(BALL_WARPS * 32) ballKernel(TickParams p, ArenaDev arena, StageScratch x, int t)
+{
+    __shared__ int wbufS[BALL_WARPS][WARP_WORDS];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int s = blockIdx.x * BALL_WARPS + warp;
+    if (s >= p.nSim) return;
+    const CarSoa cars{ p.car, (int)p.carStride };
+    const CarSoa sims{ p.sim, (int)p.simStride };
+    ballArenaStage(cars, sims, s, p.nCars, p.tick0 + t + 1, arena, wbufS[warp], lane, x.ball, (int)p.simStride);
+}
+
+__global__ void __launch_bounds__(FIN_THREADS) finishKernel(TickParams p, StageScratch x, int t, int simsPerBlock)
+{
+    const int tid = threadIdx.x;
+    const int nCars = p.nCars;
+    const int s0 = blockIdx.x * simsPerBlock;
+    const int simsHere = min(simsPerBlock, p.nSim - s0);
+    const int carsHere = simsHere * nCars;
+    const CarSoa cars{ p.car, (int)p.carStride };
+    const CarSoa sims{ p.sim, (int)p.simStride };
+    const int tick = p.tick0 + t + 1;
+    const bool lastTick = t == p.nTicks - 1;
+
+    if (tid < simsHere) ballFinishStage(cars, sims, s0 + tid, nCars, tick, x.ball, (int)p.simStride);
+    __syncthreads();
+    if (tid < carsHere)
+    {
+        const int i = s0 * nCars + tid;
+        if (!cars.n(C_DEMOED, i))
+        {
+            V3 pos = cars.v(C_POS, i), cen, vel = cars.v(C_VEL, i), ang = cars.v(C_ANG, i);
+            Q4 rot = cars.q(C_ROT, i);
+            integratePose(pos, cen, rot, vel, ang);
+            clampCarVelocity(vel, ang);
+            cars.setv(C_POS, i, pos);
+            cars.setv(C_VEL, i, vel);
+            cars.setv(C_ANG, i, ang);
+            cars.setv(C_CEN, i, cen);
+            cars.setq(C_ROT, i, rot);
+        }
+        const Controls ctl = decodeAction(p.actions, p.actionKind, i);
+        const bool respawned = finishCar(cars, i, ctl.steer, (i % nCars) >= p.nBlue, c_tables);
+        if (lastTick)
+        {
+            const unsigned bits = x.wheelBits[i];
+            int* outI = reinterpret_cast<int*>(p.carOut);
+            #pragma unroll
+            for (int w = 0; w < NUM_WHEELS; w++)
+                outI[(long long)(O_WHEEL_CON + w) * p.carStride + i] = respawned ? 0 : (int)((bits >> w) & 1u);
+            p.carOut[(long long)(O_CONTROLS + 0) * p.carStride + i] = ctl.throttle;
+            p.carOut[(long long)(O_CONTROLS + 1) * p.carStride + i] = ctl.steer;
+            p.carOut[(long long)(O_CONTROLS + 2) * p.carStride + i] = ctl.yaw;
+            p.carOut[(long long)(O_CONTROLS + 3) * p.carStride + i] = ctl.pitch;
+            p.carOut[(long long)(O_CONTROLS + 4) * p.carStride + i] = ctl.roll;
+            outI[(long long)(O_CONTROLS + 5) * p.carStride + i] = ctl.jump;
+            outI[(long long)(O_CONTROLS + 6) * p.carStride + i] = ctl.boost;
+            outI[(long long)(O_CONTROLS + 7) * p.carStride + i] = ctl.slide;
+        }
+    }
+    if (tid < simsHere) finishBall(sims, s0 + tid);
+    __syncthreads();
+    for (int it = tid; it < simsHere * NUM_BOOST_PADS; it += blockDim.x)
+    {
+        const int pad = it / simsHere;
+        const int s = s0 + (it - pad * simsHere);
+        boostPad(cars, s * nCars, nCars, sims, s, pad, c_tables);
+    }
+}
+
 }  // namespace
 
 int uploadTickTables(const Tables& t)
@@ -920,6 +1473,46 @@ int launchTick(const TickParams& p, const ArenaDev& a, void* stream)
     }
     const int blocks = (p.nSim + p.tileSims - 1) / p.tileSims;
     tickKernel<<<blocks, threads, smem, (cudaStream_t)stream>>>(p, a);
+    return (int)cudaGetLastError();
+}
+
+
+size_t stageCandSmemBytes(int hitWords)
+{
+    const int B = CAND_BLOCK;
+    size_t words = (size_t)B + B + (B + 1) + 32 + 15 * B + 7 * B + (size_t)hitWords * B;
+    size_t bytes = (words * 4 + 7) & ~(size_t)7;
+    return bytes + 8 * 4 * (size_t)B;
+}
+
+int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch& x, void* stream)
+{
+    if (p.nTicks <= 0 || p.nSim <= 0) return 0;
+    if ((long long)NCW * p.carStride >= (1LL << 31) || (long long)NSW * p.simStride >= (1LL << 31))
+        return (int)cudaErrorInvalidValue;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int n = p.nSim * p.nCars;
+    const size_t candSmem = stageCandSmemBytes(a.hitWords);
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !configured[dev])
+    {
+        const cudaError_t err = cudaFuncSetAttribute(candKernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                     64 * 1024);
+        if (err != cudaSuccess) return (int)err;
+        if (dev >= 0 && dev < 64) configured[dev] = true;
+    }
+    if (candSmem > 64 * 1024) return (int)cudaErrorInvalidValue;
+    const int simsPerFin = FIN_THREADS / p.nCars;
+    for (int t = 0; t < p.nTicks; t++)
+    {
+        candKernel<<<(n + CAND_BLOCK - 1) / CAND_BLOCK, CAND_BLOCK, candSmem, st>>>(p, a, x, t);
+        solveKernel<<<(n + SOLVE_BLOCK - 1) / SOLVE_BLOCK, SOLVE_BLOCK, 0, st>>>(p, a, x, t);
+        carCarKernel<<<(p.nSim + CC_BLOCK - 1) / CC_BLOCK, CC_BLOCK, 0, st>>>(p, t);
+        ballKernel<<<(p.nSim + BALL_WARPS - 1) / BALL_WARPS, BALL_WARPS * 32, 0, st>>>(p, a, x, t);
+        finishKernel<<<(p.nSim + simsPerFin - 1) / simsPerFin, FIN_THREADS, 0, st>>>(p, x, t, simsPerFin);
+    }
     return (int)cudaGetLastError();
 }
 

@@ -40,6 +40,17 @@ struct TickParams
     int compatFlags;        // carlb_config::compat_flags
 };
 
+// Scratch of the staged path (device arrays, word-major with the env's strides).
+struct StageScratch
+{
+    int* first;             // [carStride] first cell-list entry of the car's candidates
+    int* cnt;               // [carStride] candidate count
+    float* ray;             // [16][carStride] ray distance (4), ray normal (12)
+    unsigned* hits;         // [hitWords][carStride] SAT hit bitmask over candidates
+    unsigned* wheelBits;    // [carStride] wheels with a ray contact this tick
+    float* ball;            // [12][simStride] ball stage hand-over values
+};
+
 struct Tables;
 // Copies the game tables into this kernel's constant memory.
 int uploadTickTables(const Tables& t);
@@ -50,5 +61,8 @@ int tickThreads(int tileSims, int nCars);
 
 // Launches ceil(nSim / tileSims) CTAs on `stream`.
 int launchTick(const TickParams& p, const ArenaDev& a, void* stream);
+
+// The same ticks as a sequence of stage kernels over the state in global memory.
+int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch& x, void* stream);
 
 }  // namespace cb
