@@ -341,24 +341,49 @@ CB_D void addManifoldPoint(MPoint* p, int& count, const MPoint& point)
 }
 
 // Contacts with the floor (z = 0), ceiling (z = 2044), and side walls (x = +-4096).
+// Deepest box corner towards analytic plane k (floor, ceiling, +x wall, -x wall)
+// and its signed distance from the plane.
+CB_D void planeCorner(int k, V3 cen, Q4 rot, V3& n, V3& carPos, V3& worldCar, float& dist)
+{
+    const float offsets[4] = { 0.f, -2044.f, -4096.f, -4096.f };
+    const V3 normals[4] = { { 0.f, 0.f, 1.f }, { 0.f, 0.f, -1.f }, { 1.f, 0.f, 0.f }, { -1.f, 0.f, 0.f } };
+    n = normals[k];
+    const V3 dir = unrotate(rot, neg(n));
+    carPos = V3{ dir.x >= 0 ? CAR_HALF_X : -CAR_HALF_X, dir.y >= 0 ? CAR_HALF_Y : -CAR_HALF_Y,
+                 dir.z >= 0 ? CAR_HALF_Z : -CAR_HALF_Z };
+    worldCar = cen + rotate(rot, carPos);
+    dist = dot(n, worldCar) - offsets[k];
+}
+
 CB_D int planeManifold(V3 cen, Q4 rot, MPoint* p)
 {
     int count = 0;
-    const float offsets[4] = { 0.f, -2044.f, -4096.f, -4096.f };
-    const V3 normals[4] = { { 0.f, 0.f, 1.f }, { 0.f, 0.f, -1.f }, { 1.f, 0.f, 0.f }, { -1.f, 0.f, 0.f } };
     #pragma unroll
     for (int k = 0; k < 4; k++)
     {
-        const V3 n = normals[k];
-        const V3 dir = unrotate(rot, neg(n));
-        const V3 carPos = { dir.x >= 0 ? CAR_HALF_X : -CAR_HALF_X, dir.y >= 0 ? CAR_HALF_Y : -CAR_HALF_Y,
-                            dir.z >= 0 ? CAR_HALF_Z : -CAR_HALF_Z };
-        const V3 worldCar = cen + rotate(rot, carPos);
-        const float dist = dot(n, worldCar) - offsets[k];
+        V3 n, carPos, worldCar;
+        float dist;
+        planeCorner(k, cen, rot, n, carPos, worldCar, dist);
         if (dist < CAR_CONTACT_BREAK && !nearManifoldPoint(p, count, carPos))
             addManifoldPoint(p, count, MPoint{ carPos, worldCar - n * dist, n, dist });
     }
     return count;
+}
+
+// Whether planeManifold would add any point (the first plane within the contact
+// break always adds one).
+CB_D bool planeContactAny(V3 cen, Q4 rot)
+{
+    bool any = false;
+    #pragma unroll
+    for (int k = 0; k < 4; k++)
+    {
+        V3 n, carPos, worldCar;
+        float dist;
+        planeCorner(k, cen, rot, n, carPos, worldCar, dist);
+        any |= dist < CAR_CONTACT_BREAK;
+    }
+    return any;
 }
 
 CB_D MPoint contactToManifold(const Contact& c, V3 cen, Q4 rot)

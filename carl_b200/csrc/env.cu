@@ -79,6 +79,7 @@ struct carlb_env
     float4* triV = nullptr;
     float4* triAng = nullptr;
     float4* cellSph = nullptr;
+    float4* cellV = nullptr;
     float carReach = 0.f;
     int* cellStart = nullptr;
     int* cellTris = nullptr;
@@ -121,7 +122,7 @@ struct carlb_env
         g.simOffset = cfg.sim_offset;
         return g;
     }
-    ArenaDev arena() const { return ArenaDev{ triV, triAng, cellStart, cellTris, hitWords, cellSph, carReach }; }
+    ArenaDev arena() const { return ArenaDev{ triV, triAng, cellStart, cellTris, hitWords, cellSph, carReach, cellV }; }
     Outputs outputs() const
     {
         return Outputs{ rewards, dones, scoreDiff, episodeTicks, tScoreDiff, tEpisodeTicks, overtime, tovertime };
@@ -371,7 +372,13 @@ static carlb_status initEnv(carlb_env* p, const carlb_config* cfg)
         ECHECK(p, allocZero(p, &p->scratch.ray, (size_t)16 * p->carStride));
         ECHECK(p, allocZero(p, &p->scratch.hits, (size_t)p->hitWords * p->carStride));
         ECHECK(p, allocZero(p, &p->scratch.wheelBits, (size_t)p->carStride));
-        ECHECK(p, allocZero(p, &p->scratch.ball, (size_t)12 * p->simStride));
+        ECHECK(p, allocZero(p, &p->scratch.keys, (size_t)4 * p->carStride));
+        ECHECK(p, allocZero(p, &p->scratch.heavyBody, (size_t)18 * p->carStride));
+        ECHECK(p, allocZero(p, &p->scratch.heavyList, (size_t)p->carStride));
+        ECHECK(p, allocZero(p, &p->scratch.heavyCount, (size_t)1));
+        ECHECK(p, allocZero(p, &p->scratch.ball, (size_t)15 * p->simStride));
+        ECHECK(p, allocZero(p, &p->scratch.ballList, (size_t)p->simStride));
+        ECHECK(p, allocZero(p, &p->scratch.ballCount, (size_t)1));
     }
     p->actionCapacity = (size_t)p->nCarTotal * 32;
     {
@@ -431,6 +438,14 @@ static carlb_status initEnv(carlb_env* p, const carlb_config* cfg)
     }
     std::vector<float4> cellSph(host->cellTris.size());
     for (size_t e = 0; e < cellSph.size(); e++) cellSph[e] = triSph[host->cellTris[e]];
+    // Vertices per cell-list entry too, so a candidate's geometry is one load
+    // away from its entry index rather than behind the triangle index.
+    std::vector<float4> cellV(3 * host->cellTris.size());
+    for (size_t e = 0; e < host->cellTris.size(); e++)
+        for (int k = 0; k < 3; k++) cellV[3 * e + k] = triV[3 * (size_t)host->cellTris[e] + k];
+    ECHECK(p, allocZero(p, &p->cellV, cellV.size()));
+    ECHECK(p, cudaMemcpyAsync(p->cellV, cellV.data(), cellV.size() * sizeof(float4), cudaMemcpyHostToDevice,
+                              p->stream));
     ECHECK(p, allocZero(p, &p->cellSph, cellSph.size()));
     ECHECK(p, cudaMemcpyAsync(p->cellSph, cellSph.data(), cellSph.size() * sizeof(float4), cudaMemcpyHostToDevice,
                               p->stream));

@@ -25,6 +25,8 @@
 // operation order (the file is compiled with --fmad=false).
 #include "tick.cuh"
 
+#include <algorithm>
+
 #include <cuda_runtime.h>
 
 #include "cb_misc.cuh"
@@ -122,164 +124,198 @@ __device__ Controls decodeAction(const void* actions, int kind, long long row)
     return c;
 }
 
-// ---- ball stage, part 1: arena contacts of one sim, executed by one warp ------------------
+// ---- ball stage, part 1: arena contacts of one sim ------------------------------------------
 //
-// Per-sim values handed to part 2 (BallScratch words, one row per sim):
-// 0-2 the exported position at stage start, 3-5 posBT, 6-8 preSolveBT, 9-11 pushVel.
-constexpr int BALL_SCRATCH_WORDS = 12;
+// Per-sim values handed between the parts (15 scratch words, one row per sim):
+// 0-2 the exported position at stage start, 3-5 posBT, 6-8 preSolveBT, 9-11 pushVel,
+// 12-14 velNoExt.
 
-__device__ void ballArenaStage(const SmemSoa& cars, const SmemSoa& sims, int s, int nCars, int tick,
-                               const ArenaDev& arena, int* wbuf, int lane, float* scratch, int scratchStride)
+struct BallPre
 {
-    const int carBase = s * nCars;
+    V3 exportedPos, posBT, preSolveBT, velNoExt;
+    bool sleeping;
+};
+
+// The ball's integration inputs at stage start (include/Physics/BallArena/Solve.cuh:61-82).
+template <class T>
+CB_D BallPre ballPre(const T& sims, int s)
+{
     const V3 ballVel = sims.v(S_BVEL, s);
     const V3 ballAng = sims.v(S_BANG, s);
-    const bool sleeping = lensq(ballVel) == 0.f && lensq(ballAng) == 0.f;
-    const V3 exportedPos = sims.v(S_BPOS, s);
+    BallPre b;
+    b.sleeping = lensq(ballVel) == 0.f && lensq(ballAng) == 0.f;
+    b.exportedPos = sims.v(S_BPOS, s);
     const bool valid = sims.n(S_IVALID, s) != 0;
-
-    const V3 posBT = valid && lensq(exportedPos - sims.v(S_EPOS, s)) == 0.f ? sims.v(S_IPOS, s) : exportedPos * .02f;
+    b.posBT = valid && lensq(b.exportedPos - sims.v(S_EPOS, s)) == 0.f ? sims.v(S_IPOS, s) : b.exportedPos * .02f;
     const V3 velBT = valid && lensq(ballVel - sims.v(S_EVEL, s)) == 0.f ? sims.v(S_IVEL, s) : ballVel * .02f;
-    const V3 dampedBT = sleeping ? velBT : velBT * powf(1.f - BALL_DRAG, PHYS_DT);
-    const V3 preSolveBT = sleeping ? velBT : dampedBT + (V3{ 0.f, 0.f, GRAVITY_Z } * .02f) * PHYS_DT;
-    const V3 velNoExt = dampedBT * 50.f;
-    const V3 preSolveVel = preSolveBT * 50.f;
-    V3 pushVel = v3zero();
+    const V3 dampedBT = b.sleeping ? velBT : velBT * powf(1.f - BALL_DRAG, PHYS_DT);
+    b.preSolveBT = b.sleeping ? velBT : dampedBT + (V3{ 0.f, 0.f, GRAVITY_Z } * .02f) * PHYS_DT;
+    b.velNoExt = dampedBT * 50.f;
+    return b;
+}
 
-    if (!sleeping)
+CB_D void storeBallScratch(float* scratch, int stride, int s, const V3* v, int first, int count)
+{
+    for (int k = first; k < first + count; k++)
     {
-        // Arena triangles of the grid cells around the ball, tested across lanes.
-        const V3 center = exportedPos;
-        const V3 ext = v3fill(BALL_COLLISION_RADIUS + BALL_ARENA_CONTACT_BREAK);
-        const I3 lo = gridCell(center - ext);
-        const I3 hi = gridCell(center + ext);
-        const int nx = hi.x - lo.x + 1, ny = hi.y - lo.y + 1, nz = hi.z - lo.z + 1;
-        const int nCells = nx * ny * nz;
-        int& hitCount = wbuf[WARP_HIT_BUF];
-        if (lane == 0) hitCount = 0;
-        __syncwarp();
-        for (int q = 0; q < nCells; q++)
+        scratch[(3 * k) * stride + s] = v[k - first].x;
+        scratch[(3 * k + 1) * stride + s] = v[k - first].y;
+        scratch[(3 * k + 2) * stride + s] = v[k - first].z;
+    }
+}
+
+CB_D V3 loadBallScratch(const float* scratch, int stride, int s, int k)
+{
+    return V3{ scratch[(3 * k) * stride + s], scratch[(3 * k + 1) * stride + s], scratch[(3 * k + 2) * stride + s] };
+}
+
+// Arena contacts and solve of a moving ball, executed by one warp: triangles of
+// the grid cells around the ball are tested across lanes, the order-dependent
+// contact reduction and solve run on lane 0, which returns the push velocity.
+__device__ V3 ballArenaSolve(const SmemSoa& cars, const SmemSoa& sims, int s, int nCars, int tick,
+                             const ArenaDev& arena, int* wbuf, int lane, const BallPre& b)
+{
+    const int carBase = s * nCars;
+    const V3 ballAng = sims.v(S_BANG, s);
+    const V3 preSolveVel = b.preSolveBT * 50.f;
+    const V3 velNoExt = b.velNoExt;
+    const V3 exportedPos = b.exportedPos;
+    V3 pushVel = v3zero();
+    // Arena triangles of the grid cells around the ball, tested across lanes.
+    const V3 center = exportedPos;
+    const V3 ext = v3fill(BALL_COLLISION_RADIUS + BALL_ARENA_CONTACT_BREAK);
+    const I3 lo = gridCell(center - ext);
+    const I3 hi = gridCell(center + ext);
+    const int nx = hi.x - lo.x + 1, ny = hi.y - lo.y + 1, nz = hi.z - lo.z + 1;
+    const int nCells = nx * ny * nz;
+    int& hitCount = wbuf[WARP_HIT_BUF];
+    if (lane == 0) hitCount = 0;
+    __syncwarp();
+    for (int q = 0; q < nCells; q++)
+    {
+        const int x = lo.x + q % nx, y = lo.y + (q / nx) % ny, z = lo.z + q / (nx * ny);
+        const int cell = flatCell(I3{ x, y, z });
+        const int start = __ldg(&arena.cellStart[cell]);
+        const int end = __ldg(&arena.cellStart[cell + 1]);
+        for (int e = start + lane; e < end; e += 32)
         {
-            const int x = lo.x + q % nx, y = lo.y + (q / nx) % ny, z = lo.z + q / (nx * ny);
-            const int cell = flatCell(I3{ x, y, z });
-            const int start = __ldg(&arena.cellStart[cell]);
-            const int end = __ldg(&arena.cellStart[cell + 1]);
-            for (int e = start + lane; e < end; e += 32)
+            // A triangle beyond the contact radius (plus 1 uu) cannot touch the ball.
+            const float4 sph = __ldg(&arena.cellSph[e]);
+            const float dx = sph.x - center.x, dy = sph.y - center.y, dz = sph.z - center.z;
+            const float rr = sph.w + (BALL_COLLISION_RADIUS + BALL_ARENA_CONTACT_BREAK + 1.f);
+            if (dx * dx + dy * dy + dz * dz > rr * rr) continue;
+            const int tri = __ldg(&arena.cellTris[e]);
+            V3 v0, v1, v2;
+            int flags;
+            loadTri(arena, tri, v0, v1, v2, flags);
+            BallContact c;
+            if (sphereTriangle(center, BALL_COLLISION_RADIUS, v0, v1, v2, c))
             {
-                // A triangle beyond the contact radius (plus 1 uu) cannot touch the ball.
-                const float4 sph = __ldg(&arena.cellSph[e]);
-                const float dx = sph.x - center.x, dy = sph.y - center.y, dz = sph.z - center.z;
-                const float rr = sph.w + (BALL_COLLISION_RADIUS + BALL_ARENA_CONTACT_BREAK + 1.f);
-                if (dx * dx + dy * dy + dz * dz > rr * rr) continue;
-                const int tri = __ldg(&arena.cellTris[e]);
+                const int slot = atomicAdd(&hitCount, 1);
+                if (slot < WARP_HIT_BUF) wbuf[slot] = tri;
+            }
+        }
+    }
+    __syncwarp();
+
+    if (lane == 0)
+    {
+        BallContact set[4];
+        int count = 0;
+        const int n = hitCount;
+        if (n <= WARP_HIT_BUF)
+        {
+            // Ascending, de-duplicated triangle order (the reference merges the
+            // per-cell lists in triangle order and skips repeats).
+            for (int i = 1; i < n; i++)
+            {
+                const int v = wbuf[i];
+                int j = i - 1;
+                while (j >= 0 && wbuf[j] > v)
+                {
+                    wbuf[j + 1] = wbuf[j];
+                    j--;
+                }
+                wbuf[j + 1] = v;
+            }
+            int last = -1;
+            for (int i = 0; i < n; i++)
+            {
+                const int tri = wbuf[i];
+                if (tri == last) continue;
+                last = tri;
                 V3 v0, v1, v2;
                 int flags;
                 loadTri(arena, tri, v0, v1, v2, flags);
                 BallContact c;
-                if (sphereTriangle(center, BALL_COLLISION_RADIUS, v0, v1, v2, c))
-                {
-                    const int slot = atomicAdd(&hitCount, 1);
-                    if (slot < WARP_HIT_BUF) wbuf[slot] = tri;
-                }
+                sphereTriangle(center, BALL_COLLISION_RADIUS, v0, v1, v2, c);
+                insertBallContact(set, count, c, center, v0, v1, v2, triAngles(arena, tri));
             }
         }
-        __syncwarp();
-
-        if (lane == 0)
+        else
         {
-            BallContact set[4];
-            int count = 0;
-            const int n = hitCount;
-            if (n <= WARP_HIT_BUF)
+            // Too many hits to buffer: walk the union of the cell lists in
+            // ascending triangle order directly.
+            int cursor = -1;
+            while (true)
             {
-                // Ascending, de-duplicated triangle order (the reference merges the
-                // per-cell lists in triangle order and skips repeats).
-                for (int i = 1; i < n; i++)
+                int next = 0x7fffffff;
+                for (int q = 0; q < nCells; q++)
                 {
-                    const int v = wbuf[i];
-                    int j = i - 1;
-                    while (j >= 0 && wbuf[j] > v)
+                    const int x = lo.x + q % nx, y = lo.y + (q / nx) % ny, z = lo.z + q / (nx * ny);
+                    const int cell = flatCell(I3{ x, y, z });
+                    for (int e = __ldg(&arena.cellStart[cell]); e < __ldg(&arena.cellStart[cell + 1]); e++)
                     {
-                        wbuf[j + 1] = wbuf[j];
-                        j--;
-                    }
-                    wbuf[j + 1] = v;
-                }
-                int last = -1;
-                for (int i = 0; i < n; i++)
-                {
-                    const int tri = wbuf[i];
-                    if (tri == last) continue;
-                    last = tri;
-                    V3 v0, v1, v2;
-                    int flags;
-                    loadTri(arena, tri, v0, v1, v2, flags);
-                    BallContact c;
-                    sphereTriangle(center, BALL_COLLISION_RADIUS, v0, v1, v2, c);
-                    insertBallContact(set, count, c, center, v0, v1, v2, triAngles(arena, tri));
-                }
-            }
-            else
-            {
-                // Too many hits to buffer: walk the union of the cell lists in
-                // ascending triangle order directly.
-                int cursor = -1;
-                while (true)
-                {
-                    int next = 0x7fffffff;
-                    for (int q = 0; q < nCells; q++)
-                    {
-                        const int x = lo.x + q % nx, y = lo.y + (q / nx) % ny, z = lo.z + q / (nx * ny);
-                        const int cell = flatCell(I3{ x, y, z });
-                        for (int e = __ldg(&arena.cellStart[cell]); e < __ldg(&arena.cellStart[cell + 1]); e++)
+                        const int tri = __ldg(&arena.cellTris[e]);
+                        if (tri > cursor)
                         {
-                            const int tri = __ldg(&arena.cellTris[e]);
-                            if (tri > cursor)
-                            {
-                                if (tri < next) next = tri;
-                                break;  // cell lists are ascending
-                            }
+                            if (tri < next) next = tri;
+                            break;  // cell lists are ascending
                         }
                     }
-                    if (next == 0x7fffffff) break;
-                    cursor = next;
-                    V3 v0, v1, v2;
-                    int flags;
-                    loadTri(arena, next, v0, v1, v2, flags);
-                    BallContact c;
-                    if (sphereTriangle(center, BALL_COLLISION_RADIUS, v0, v1, v2, c))
-                        insertBallContact(set, count, c, center, v0, v1, v2, triAngles(arena, next));
                 }
+                if (next == 0x7fffffff) break;
+                cursor = next;
+                V3 v0, v1, v2;
+                int flags;
+                loadTri(arena, next, v0, v1, v2, flags);
+                BallContact c;
+                if (sphereTriangle(center, BALL_COLLISION_RADIUS, v0, v1, v2, c))
+                    insertBallContact(set, count, c, center, v0, v1, v2, triAngles(arena, next));
             }
-
-            bool wasHit = false;
-            for (int k = 0; k < nCars; k++)
-            {
-                const int hitTick = cars.n(C_BALL_HIT_TICK, carBase + k);
-                wasHit |= hitTick >= 0 && tick > 0 && hitTick == tick - 1;
-            }
-            BallBody body;
-            body.pos = center;
-            body.vel = preSolveVel;
-            body.velNoExt = velNoExt;
-            body.ang = ballAng;
-            body.deltaVel = body.deltaAng = body.pushVel = body.pushAng = v3zero();
-            solveBallArena(body, set, count, wasHit);
-            sims.setv(S_BVEL, s, body.vel);
-            sims.setv(S_BANG, s, body.ang);
-            pushVel = body.pushVel;
         }
+
+        bool wasHit = false;
+        for (int k = 0; k < nCars; k++)
+        {
+            const int hitTick = cars.n(C_BALL_HIT_TICK, carBase + k);
+            wasHit |= hitTick >= 0 && tick > 0 && hitTick == tick - 1;
+        }
+        BallBody body;
+        body.pos = center;
+        body.vel = preSolveVel;
+        body.velNoExt = velNoExt;
+        body.ang = ballAng;
+        body.deltaVel = body.deltaAng = body.pushVel = body.pushAng = v3zero();
+        solveBallArena(body, set, count, wasHit);
+        sims.setv(S_BVEL, s, body.vel);
+        sims.setv(S_BANG, s, body.ang);
+        pushVel = body.pushVel;
     }
+    return pushVel;
+}
+
+// Part 1 for one sim on one warp (fused path): prelude, arena contacts, hand-over.
+__device__ void ballArenaStage(const SmemSoa& cars, const SmemSoa& sims, int s, int nCars, int tick,
+                               const ArenaDev& arena, int* wbuf, int lane, float* scratch, int scratchStride)
+{
+    const BallPre b = ballPre(sims, s);
+    V3 pushVel = v3zero();
+    if (!b.sleeping) pushVel = ballArenaSolve(cars, sims, s, nCars, tick, arena, wbuf, lane, b);
     if (lane == 0)
     {
-        const V3 out[4] = { exportedPos, posBT, preSolveBT, pushVel };
-        #pragma unroll
-        for (int k = 0; k < 4; k++)
-        {
-            scratch[(3 * k) * scratchStride + s] = out[k].x;
-            scratch[(3 * k + 1) * scratchStride + s] = out[k].y;
-            scratch[(3 * k + 2) * scratchStride + s] = out[k].z;
-        }
+        const V3 out[5] = { b.exportedPos, b.posBT, b.preSolveBT, pushVel, b.velNoExt };
+        storeBallScratch(scratch, scratchStride, s, out, 0, 5);
     }
     __syncwarp();
 }
@@ -889,22 +925,26 @@ __global__ void __launch_bounds__(256) tickKernel(TickParams p, ArenaDev arena)
 // Staged path: the same tick as a sequence of kernels over the state in global memory
 // (resident in L2 between stages), so each stage runs at its own occupancy and no warp
 // waits on a CTA barrier for unrelated work.  Per tick:
-//   candKernel     begin step, broadphase, (car, candidate) rays + SAT, ray finish, controls
-//   solveKernel    suspension, plane + mesh manifold, car-arena solve
-//   carCarKernel   car-car pairs, one thread per sim with a pair in reach
-//   ballKernel     ball arena contacts, one warp per sim
+//   flatKernel     begin step, broadphase, (car, candidate) wheel rays + SAT, per CTA of cars
+//   rayCtlKernel   ray finish (arena hit, other cars' boxes, ball), controls
+//   suspKernel     suspension; cars that may touch a plane or the mesh are listed
+//   contactKernel  plane + mesh manifold and car-arena solve of the listed cars
+//   carCarKernel   ball prelude (moving balls are listed), car-car pairs per sim
+//   ballKernel     ball arena contacts, one warp per listed ball
 //   finishKernel   ball vs cars + integration + goal, car integration + finish, boost pads
 // =========================================================================================
 
-constexpr int CAND_BLOCK = 128;   // cars per candKernel CTA
-constexpr int SOLVE_BLOCK = 128;  // cars per solveKernel CTA
+constexpr int CAND_BLOCK = 128;   // cars per candKernel CTA (car numbers fit the uint8 item map)
+constexpr int CAND_MAP_CAP = 12288;  // items per CTA resolved through the shared item -> car map
+constexpr int RAY_BLOCK = 128;    // cars per rayCtlKernel CTA
+constexpr int SOLVE_BLOCK = 128;  // cars per suspKernel / contactKernel CTA
 constexpr int CC_BLOCK = 128;     // sims per carCarKernel CTA
 constexpr int BALL_WARPS = 4;     // sims (warps) per ballKernel CTA
 constexpr int FIN_THREADS = 256;  // threads per finishKernel CTA
 
 using CarSoa = Soa<int>;  // int indexing: NCW * carStride < 2^31 is checked at launch
 
-__global__ void __launch_bounds__(CAND_BLOCK) candKernel(TickParams p, ArenaDev arena, StageScratch x, int t)
+__global__ void __launch_bounds__(CAND_BLOCK) flatKernel(TickParams p, ArenaDev arena, StageScratch x, int t)
 {
     extern __shared__ __align__(16) float sm[];
     const int B = CAND_BLOCK, HW = arena.hitWords;
@@ -917,6 +957,7 @@ __global__ void __launch_bounds__(CAND_BLOCK) candKernel(TickParams p, ArenaDev 
     unsigned* hitS = reinterpret_cast<unsigned*>(poseS + 7 * B);  // [HW][B]
     const size_t keyOff = ((size_t)(hitS + HW * B) - (size_t)sm + 7) & ~(size_t)7;
     unsigned long long* keyS = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(sm) + keyOff);  // [4][B]
+    unsigned char* mapS = reinterpret_cast<unsigned char*>(keyS + 4 * B);  // [CAND_MAP_CAP] item -> car
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int n = p.nSim * p.nCars;
@@ -926,7 +967,6 @@ __global__ void __launch_bounds__(CAND_BLOCK) candKernel(TickParams p, ArenaDev 
     const bool valid = tid < here;
     const CarSoa cars{ p.car, (int)p.carStride };
     const CarSoa sims{ p.sim, (int)p.simStride };
-    const int tick = p.tick0 + t + 1;
     const bool lastTick = t == p.nTicks - 1;
 
     V3 cen = v3zero(), up = v3zero();
@@ -996,6 +1036,9 @@ __global__ void __launch_bounds__(CAND_BLOCK) candKernel(TickParams p, ArenaDev 
         if (warp > 0) v += wsumS[warp - 1];
         preS[tid + 1] = v;
         if (tid == 0) preS[0] = 0;
+        // Item -> car map for the first CAND_MAP_CAP items (later items search preS).
+        const int cnt = cntS[tid];
+        for (int k = v - cnt; k < v && k < CAND_MAP_CAP; k++) mapS[k] = (unsigned char)tid;
     }
     __syncthreads();
 
@@ -1003,14 +1046,22 @@ __global__ void __launch_bounds__(CAND_BLOCK) candKernel(TickParams p, ArenaDev 
     const int total = preS[here];
     for (int it = tid; it < total; it += B)
     {
-        int lo = 0, hi = here - 1;
-        while (lo < hi)
+        int c;
+        if (it < CAND_MAP_CAP)
         {
-            const int mid = (lo + hi + 1) >> 1;
-            if (preS[mid] <= it) lo = mid;
-            else hi = mid - 1;
+            c = mapS[it];
         }
-        const int c = lo;
+        else
+        {
+            int lo = 0, hi = here - 1;
+            while (lo < hi)
+            {
+                const int mid = (lo + hi + 1) >> 1;
+                if (preS[mid] <= it) lo = mid;
+                else hi = mid - 1;
+            }
+            c = lo;
+        }
         const int k = it - preS[c];
         const int e = firstS[c] + k;
         const V3 cc = { poseS[0 * B + c], poseS[1 * B + c], poseS[2 * B + c] };
@@ -1020,10 +1071,11 @@ __global__ void __launch_bounds__(CAND_BLOCK) candKernel(TickParams p, ArenaDev 
             const float rr = sph.w + arena.carReach;
             if (dx * dx + dy * dy + dz * dz > rr * rr) continue;
         }
-        const int tri = __ldg(&arena.cellTris[e]);
-        V3 v0, v1, v2;
-        int flags;
-        loadTri(arena, tri, v0, v1, v2, flags);
+        const float4 q0 = __ldg(&arena.cellV[3 * e]);
+        const float4 q1 = __ldg(&arena.cellV[3 * e + 1]);
+        const float4 q2 = __ldg(&arena.cellV[3 * e + 2]);
+        const V3 v0 = { q0.x, q0.y, q0.z }, v1 = { q1.x, q1.y, q1.z }, v2 = { q2.x, q2.y, q2.z };
+        const int flags = __float_as_int(q0.w);
 
         const V3 dir = { rsS[12 * B + c], rsS[13 * B + c], rsS[14 * B + c] };
         const V3 e1 = v1 - v0;
@@ -1057,6 +1109,24 @@ __global__ void __launch_bounds__(CAND_BLOCK) candKernel(TickParams p, ArenaDev 
     }
     __syncthreads();
     if (!valid) return;
+    x.first[i] = firstS[tid];
+    x.cnt[i] = cntS[tid];
+    for (int h = 0; h < HW; h++) x.hits[(long long)h * p.carStride + i] = hitS[h * B + tid];
+    #pragma unroll
+    for (int w = 0; w < NUM_WHEELS; w++) x.keys[(long long)w * p.carStride + i] = keyS[w * B + tid];
+}
+
+__global__ void __launch_bounds__(RAY_BLOCK) rayCtlKernel(TickParams p, ArenaDev arena, StageScratch x, int t)
+{
+    const int n = p.nSim * p.nCars;
+    const int i = blockIdx.x * RAY_BLOCK + threadIdx.x;
+    if (i >= n) return;
+    const CarSoa cars{ p.car, (int)p.carStride };
+    const CarSoa sims{ p.sim, (int)p.simStride };
+    const bool lastTick = t == p.nTicks - 1;
+    const V3 cen = cars.v(C_CEN, i);
+    const Q4 rot = cars.q(C_ROT, i);
+    const V3 up = rotate(rot, axisVec(2));
 
     // Finish the wheel rays: arena hit, other cars' boxes (in car order), ball.
     const V3 dir = neg(up);
@@ -1064,12 +1134,12 @@ __global__ void __launch_bounds__(CAND_BLOCK) candKernel(TickParams p, ArenaDev 
     V3 rayNormal[NUM_WHEELS];
     int src[NUM_WHEELS];
     V3 start[NUM_WHEELS];
-    const int cellFirst = firstS[tid];
+    const int cellFirst = x.first[i];
     #pragma unroll
     for (int w = 0; w < NUM_WHEELS; w++)
     {
-        start[w] = V3{ rsS[(3 * w) * B + tid], rsS[(3 * w + 1) * B + tid], rsS[(3 * w + 2) * B + tid] };
-        const unsigned long long key = keyS[w * B + tid];
+        start[w] = cen + rotate(rot, suspConnection(w));
+        const unsigned long long key = x.keys[(long long)w * p.carStride + i];
         const unsigned cand = (unsigned)(key & 0xffffffffu);
         if (cand != 0xffffffffu)
         {
@@ -1163,9 +1233,6 @@ __global__ void __launch_bounds__(CAND_BLOCK) candKernel(TickParams p, ArenaDev 
     for (int w = 0; w < NUM_WHEELS; w++)
         if (src[w] != WHEEL_NONE && rayDist[w] <= rayLen(w)) wheelBits |= 1u << w;
     x.wheelBits[i] = wheelBits;
-    x.first[i] = cellFirst;
-    x.cnt[i] = cntS[tid];
-    for (int h = 0; h < HW; h++) x.hits[(long long)h * p.carStride + i] = hitS[h * B + tid];
     #pragma unroll
     for (int w = 0; w < NUM_WHEELS; w++)
     {
@@ -1200,42 +1267,18 @@ __global__ void __launch_bounds__(CAND_BLOCK) candKernel(TickParams p, ArenaDev 
     storeSusp(cars, i, su);
 }
 
-__global__ void __launch_bounds__(SOLVE_BLOCK) solveKernel(TickParams p, ArenaDev arena, StageScratch x, int t)
+__global__ void __launch_bounds__(SOLVE_BLOCK) suspKernel(TickParams p, ArenaDev arena, StageScratch x, int t)
 {
-    __shared__ int orderS[SOLVE_BLOCK];
-    __shared__ int countS[2];
-    const int tid = threadIdx.x;
     const int n = p.nSim * p.nCars;
-    const int first = blockIdx.x * SOLVE_BLOCK;
-    const int here = min(SOLVE_BLOCK, n - first);
+    const int i = blockIdx.x * SOLVE_BLOCK + threadIdx.x;
+    if (i >= n) return;
     const CarSoa cars{ p.car, (int)p.carStride };
     const int tick = p.tick0 + t + 1;
     const bool lastTick = t == p.nTicks - 1;
     const int HW = arena.hitWords;
-
-    // Cars likely to have mesh or plane contacts first, so the long contact path
-    // runs in as few warps as possible (cars are independent in this stage).
-    if (tid < 2) countS[tid] = 0;
-    __syncthreads();
-    if (tid < here)
-    {
-        const int i = first + tid;
-        bool heavy = false;
-        if (!cars.n(C_DEMOED, i))
-        {
-            heavy = cars.n(C_MAN_COUNT, i) > 0;
-            for (int h = 0; h < HW && !heavy; h++) heavy = x.hits[(long long)h * p.carStride + i] != 0u;
-        }
-        const int slot = heavy ? atomicAdd(&countS[0], 1) : here - 1 - atomicAdd(&countS[1], 1);
-        orderS[slot] = i;
-    }
-    __syncthreads();
-    if (tid >= here) return;
-    const int i = orderS[tid];
-
-    const V3 cen = cars.v(C_CEN, i);
-    const Q4 rot = cars.q(C_ROT, i);
     const int cellFirst = x.first[i];
+    bool anyHit = false;
+    for (int h = 0; h < HW; h++) anyHit |= x.hits[(long long)h * p.carStride + i] != 0u;
     if (lastTick && p.diagCar)
     {
         p.diagCar[1 * p.carStride + i] = x.cnt[i];
@@ -1272,56 +1315,6 @@ __global__ void __launch_bounds__(SOLVE_BLOCK) solveKernel(TickParams p, ArenaDe
     }
     applySuspension(body, su, lat, lon, rayDist, rayNormal, cars.n(C_MAN_COUNT, i), cars.v(C_MAN_N0, i), tick,
                     (p.compatFlags & 1) != 0);
-
-    MPoint pts[MAX_CAR_MANIFOLD_POINTS];
-    int count = planeManifold(cen, rot, pts);
-    const int planeCount = count;
-    Contact best{};
-    float bestDist = 3.402823466e+38f;
-    int bestTri = -1;
-    int seen = 0;
-    for (int h = 0; h < HW && seen < MAX_CAR_TRI_PAIRS; h++)
-    {
-        for (unsigned m = x.hits[(long long)h * p.carStride + i]; m && seen < MAX_CAR_TRI_PAIRS; m &= m - 1)
-        {
-            seen++;
-            const int k = h * 32 + __ffs(m) - 1;
-            const int tri = __ldg(&arena.cellTris[cellFirst + k]);
-            V3 v0, v1, v2;
-            int flags;
-            loadTri(arena, tri, v0, v1, v2, flags);
-            const LocalTri lt = localTriangle(cen, rot, v0, v1, v2);
-            const Sat sat = carTriSat(lt);
-            pairContacts(lt, sat, [&](const Contact& c) {
-                if (nearManifoldPoint(pts, planeCount, c.carPos)) return;
-                const float d = -c.depth;
-                if (d < bestDist)
-                {
-                    bestDist = d;
-                    best = c;
-                    bestTri = tri;
-                }
-            });
-        }
-    }
-    if (bestTri >= 0)
-    {
-        V3 v0, v1, v2;
-        int flags;
-        loadTri(arena, bestTri, v0, v1, v2, flags);
-        adjustInternalEdge(localTriangle(cen, rot, v0, v1, v2), triAngles(arena, bestTri), best);
-        addManifoldPoint(pts, count, contactToManifold(best, cen, rot));
-    }
-    if (count > 0)
-    {
-        solveCarManifold(body, pts, count);
-        integrateSplitCorrection(body);
-    }
-    cars.n(C_MAN_COUNT, i) = count;
-    cars.setv(C_MAN_N0, i, count > 0 ? pts[0].worldNormal : v3zero());
-    body.vel = body.vel + body.extVel + body.deltaVel;
-    body.ang = body.ang + body.extAng + body.deltaAng;
-    storeCarBody(cars, i, body);
     storeSusp(cars, i, su);
     #pragma unroll
     for (int w = 0; w < NUM_WHEELS; w++)
@@ -1329,9 +1322,104 @@ __global__ void __launch_bounds__(SOLVE_BLOCK) solveKernel(TickParams p, ArenaDe
         cars.f(C_LAT + w, i) = lat[w];
         cars.f(C_LON + w, i) = lon[w];
     }
+    if (anyHit || planeContactAny(body.cen, body.rot))
+    {
+        // Plane or mesh contacts possible: the velocities after the suspension go
+        // to the contact kernel, which builds the manifold and solves it.
+        const V3 hv[6] = { body.vel, body.ang, body.extVel, body.extAng, body.deltaVel, body.deltaAng };
+        #pragma unroll
+        for (int k = 0; k < 6; k++)
+        {
+            x.heavyBody[(long long)(3 * k) * p.carStride + i] = hv[k].x;
+            x.heavyBody[(long long)(3 * k + 1) * p.carStride + i] = hv[k].y;
+            x.heavyBody[(long long)(3 * k + 2) * p.carStride + i] = hv[k].z;
+        }
+        x.heavyList[atomicAdd(x.heavyCount, 1)] = i;
+        return;
+    }
+    cars.n(C_MAN_COUNT, i) = 0;
+    cars.setv(C_MAN_N0, i, v3zero());
+    cars.setv(C_VEL, i, body.vel + body.extVel + body.deltaVel);
+    cars.setv(C_ANG, i, body.ang + body.extAng + body.deltaAng);
 }
 
-__global__ void __launch_bounds__(CC_BLOCK) carCarKernel(TickParams p, int t)
+__global__ void __launch_bounds__(SOLVE_BLOCK) contactKernel(TickParams p, ArenaDev arena, StageScratch x, int t)
+{
+    const int count = *x.heavyCount;
+    const CarSoa cars{ p.car, (int)p.carStride };
+    const int HW = arena.hitWords;
+    for (int j = blockIdx.x * SOLVE_BLOCK + threadIdx.x; j < count; j += gridDim.x * SOLVE_BLOCK)
+    {
+        const int i = x.heavyList[j];
+        Body body = loadCarBody(cars, i);
+        V3 hv[6];
+        #pragma unroll
+        for (int k = 0; k < 6; k++)
+            hv[k] = V3{ x.heavyBody[(long long)(3 * k) * p.carStride + i], x.heavyBody[(long long)(3 * k + 1) * p.carStride + i],
+                        x.heavyBody[(long long)(3 * k + 2) * p.carStride + i] };
+        body.vel = hv[0];
+        body.ang = hv[1];
+        body.extVel = hv[2];
+        body.extAng = hv[3];
+        body.deltaVel = hv[4];
+        body.deltaAng = hv[5];
+        const V3 cen = body.cen;
+        const Q4 rot = body.rot;
+        const int cellFirst = x.first[i];
+
+        MPoint pts[MAX_CAR_MANIFOLD_POINTS];
+        int cnt = planeManifold(cen, rot, pts);
+        const int planeCount = cnt;
+        Contact best{};
+        float bestDist = 3.402823466e+38f;
+        int bestTri = -1;
+        int seen = 0;
+        for (int h = 0; h < HW && seen < MAX_CAR_TRI_PAIRS; h++)
+        {
+            for (unsigned m = x.hits[(long long)h * p.carStride + i]; m && seen < MAX_CAR_TRI_PAIRS; m &= m - 1)
+            {
+                seen++;
+                const int k = h * 32 + __ffs(m) - 1;
+                const int tri = __ldg(&arena.cellTris[cellFirst + k]);
+                V3 v0, v1, v2;
+                int flags;
+                loadTri(arena, tri, v0, v1, v2, flags);
+                const LocalTri lt = localTriangle(cen, rot, v0, v1, v2);
+                const Sat sat = carTriSat(lt);
+                pairContacts(lt, sat, [&](const Contact& c) {
+                    if (nearManifoldPoint(pts, planeCount, c.carPos)) return;
+                    const float d = -c.depth;
+                    if (d < bestDist)
+                    {
+                        bestDist = d;
+                        best = c;
+                        bestTri = tri;
+                    }
+                });
+            }
+        }
+        if (bestTri >= 0)
+        {
+            V3 v0, v1, v2;
+            int flags;
+            loadTri(arena, bestTri, v0, v1, v2, flags);
+            adjustInternalEdge(localTriangle(cen, rot, v0, v1, v2), triAngles(arena, bestTri), best);
+            addManifoldPoint(pts, cnt, contactToManifold(best, cen, rot));
+        }
+        if (cnt > 0)
+        {
+            solveCarManifold(body, pts, cnt);
+            integrateSplitCorrection(body);
+        }
+        cars.n(C_MAN_COUNT, i) = cnt;
+        cars.setv(C_MAN_N0, i, cnt > 0 ? pts[0].worldNormal : v3zero());
+        body.vel = body.vel + body.extVel + body.deltaVel;
+        body.ang = body.ang + body.extAng + body.deltaAng;
+        storeCarBody(cars, i, body);
+    }
+}
+
+__global__ void __launch_bounds__(CC_BLOCK) carCarKernel(TickParams p, StageScratch x, int t)
 {
     __shared__ int activeS[CC_BLOCK];
     __shared__ int nActive;
@@ -1346,6 +1434,15 @@ __global__ void __launch_bounds__(CC_BLOCK) carCarKernel(TickParams p, int t)
     __syncthreads();
     if (s < p.nSim)
     {
+        // Ball stage prelude (reads only the ball, which car-car leaves alone):
+        // hand-over values for every sim, and the list of moving balls, the only
+        // ones with arena work.
+        const CarSoa sims{ p.sim, (int)p.simStride };
+        const BallPre bp = ballPre(sims, s);
+        const V3 out[5] = { bp.exportedPos, bp.posBT, bp.preSolveBT, v3zero(), bp.velNoExt };
+        storeBallScratch(x.ball, (int)p.simStride, s, out, 0, 5);
+        if (!bp.sleeping) x.ballList[atomicAdd(x.ballCount, 1)] = s;
+
         const int sb = s * nCars;
         bool gate = false;
         for (int a = 0; a < nCars - 1 && !gate; a++)
@@ -1372,11 +1469,23 @@ __global__ void __launch_bounds__(BALL_WARPS * 32) ballKernel(TickParams p, Aren
 {
     __shared__ int wbufS[BALL_WARPS][WARP_WORDS];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int s = blockIdx.x * BALL_WARPS + warp;
-    if (s >= p.nSim) return;
     const CarSoa cars{ p.car, (int)p.carStride };
     const CarSoa sims{ p.sim, (int)p.simStride };
-    ballArenaStage(cars, sims, s, p.nCars, p.tick0 + t + 1, arena, wbufS[warp], lane, x.ball, (int)p.simStride);
+    const int stride = (int)p.simStride;
+    const int count = *x.ballCount;
+    for (int j = blockIdx.x * BALL_WARPS + warp; j < count; j += gridDim.x * BALL_WARPS)
+    {
+        const int s = x.ballList[j];
+        BallPre b;
+        b.sleeping = false;
+        b.exportedPos = loadBallScratch(x.ball, stride, s, 0);
+        b.posBT = loadBallScratch(x.ball, stride, s, 1);
+        b.preSolveBT = loadBallScratch(x.ball, stride, s, 2);
+        b.velNoExt = loadBallScratch(x.ball, stride, s, 4);
+        const V3 pushVel = ballArenaSolve(cars, sims, s, p.nCars, p.tick0 + t + 1, arena, wbufS[warp], lane, b);
+        if (lane == 0) storeBallScratch(x.ball, stride, s, &pushVel, 3, 1);
+        __syncwarp();
+    }
 }
 
 __global__ void __launch_bounds__(FIN_THREADS) finishKernel(TickParams p, StageScratch x, int t, int simsPerBlock)
@@ -1391,6 +1500,12 @@ __global__ void __launch_bounds__(FIN_THREADS) finishKernel(TickParams p, StageS
     const int tick = p.tick0 + t + 1;
     const bool lastTick = t == p.nTicks - 1;
 
+    if (blockIdx.x == 0 && tid == 0)
+    {
+        // The per-tick work lists are consumed; empty them for the next tick.
+        *x.ballCount = 0;
+        *x.heavyCount = 0;
+    }
     if (tid < simsHere) ballFinishStage(cars, sims, s0 + tid, nCars, tick, x.ball, (int)p.simStride);
     __syncthreads();
     if (tid < carsHere)
@@ -1482,7 +1597,7 @@ size_t stageCandSmemBytes(int hitWords)
     const int B = CAND_BLOCK;
     size_t words = (size_t)B + B + (B + 1) + 32 + 15 * B + 7 * B + (size_t)hitWords * B;
     size_t bytes = (words * 4 + 7) & ~(size_t)7;
-    return bytes + 8 * 4 * (size_t)B;
+    return bytes + 8 * 4 * (size_t)B + CAND_MAP_CAP;
 }
 
 int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch& x, void* stream)
@@ -1498,19 +1613,26 @@ int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch&
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !configured[dev])
     {
-        const cudaError_t err = cudaFuncSetAttribute(candKernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        const cudaError_t err = cudaFuncSetAttribute(flatKernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                      64 * 1024);
         if (err != cudaSuccess) return (int)err;
         if (dev >= 0 && dev < 64) configured[dev] = true;
     }
     if (candSmem > 64 * 1024) return (int)cudaErrorInvalidValue;
     const int simsPerFin = FIN_THREADS / p.nCars;
+    // Warps loop over the moving balls; enough CTAs for a few per SM, never more than the sims.
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int ballBlocks = std::max(1, std::min((p.nSim + BALL_WARPS - 1) / BALL_WARPS, sms * 8));
+    const int contactBlocks = std::max(1, std::min((n + SOLVE_BLOCK - 1) / SOLVE_BLOCK, sms * 4));
     for (int t = 0; t < p.nTicks; t++)
     {
-        candKernel<<<(n + CAND_BLOCK - 1) / CAND_BLOCK, CAND_BLOCK, candSmem, st>>>(p, a, x, t);
-        solveKernel<<<(n + SOLVE_BLOCK - 1) / SOLVE_BLOCK, SOLVE_BLOCK, 0, st>>>(p, a, x, t);
-        carCarKernel<<<(p.nSim + CC_BLOCK - 1) / CC_BLOCK, CC_BLOCK, 0, st>>>(p, t);
-        ballKernel<<<(p.nSim + BALL_WARPS - 1) / BALL_WARPS, BALL_WARPS * 32, 0, st>>>(p, a, x, t);
+        flatKernel<<<(n + CAND_BLOCK - 1) / CAND_BLOCK, CAND_BLOCK, candSmem, st>>>(p, a, x, t);
+        rayCtlKernel<<<(n + RAY_BLOCK - 1) / RAY_BLOCK, RAY_BLOCK, 0, st>>>(p, a, x, t);
+        suspKernel<<<(n + SOLVE_BLOCK - 1) / SOLVE_BLOCK, SOLVE_BLOCK, 0, st>>>(p, a, x, t);
+        contactKernel<<<contactBlocks, SOLVE_BLOCK, 0, st>>>(p, a, x, t);
+        carCarKernel<<<(p.nSim + CC_BLOCK - 1) / CC_BLOCK, CC_BLOCK, 0, st>>>(p, x, t);
+        ballKernel<<<ballBlocks, BALL_WARPS * 32, 0, st>>>(p, a, x, t);
         finishKernel<<<(p.nSim + simsPerFin - 1) / simsPerFin, FIN_THREADS, 0, st>>>(p, x, t, simsPerFin);
     }
     return (int)cudaGetLastError();

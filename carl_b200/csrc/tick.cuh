@@ -20,6 +20,7 @@ struct ArenaDev
     const float4* cellSph;  // [cellStart[NUM_CELLS]]: bounding sphere of cellTris[e] (centre xyz, radius w),
                             // radius rounded up
     float carReach;         // radius around a car's box centre that holds its box and wheel rays, plus margin
+    const float4* cellV;    // [3 * cellStart[NUM_CELLS]]: vertices of cellTris[e] (flags in vertex 0's w)
 };
 
 struct TickParams
@@ -48,7 +49,13 @@ struct StageScratch
     float* ray;             // [16][carStride] ray distance (4), ray normal (12)
     unsigned* hits;         // [hitWords][carStride] SAT hit bitmask over candidates
     unsigned* wheelBits;    // [carStride] wheels with a ray contact this tick
-    float* ball;            // [12][simStride] ball stage hand-over values
+    unsigned long long* keys;  // [4][carStride] wheel ray minimum (distance bits, candidate)
+    float* heavyBody;       // [18][carStride] velocities after the suspension of listed cars
+    int* heavyList;         // [carStride] cars with possible plane / mesh contacts, this tick
+    int* heavyCount;        // [1] entries of heavyList; zero between ticks
+    float* ball;            // [15][simStride] ball stage hand-over values
+    int* ballList;          // [simStride] sims whose ball is moving (arena work), this tick
+    int* ballCount;         // [1] entries of ballList; zero between ticks
 };
 
 struct Tables;
