@@ -89,6 +89,10 @@ struct carlb_env
     // fused per-tile kernel (CARLB_TICK_PATH=fused, read at create).
     bool staged = true;
     StageScratch scratch{};
+    int groups = 2;
+    cudaStream_t groupStream[8] = {};
+    cudaEvent_t groupJoin[8] = {};
+    cudaEvent_t evFork = nullptr;
 
     float *obs = nullptr, *tobs = nullptr, *packed = nullptr, *tpacked = nullptr, *rewards = nullptr;
     uint8_t *dones = nullptr, *overtime = nullptr, *tovertime = nullptr;
@@ -121,6 +125,18 @@ struct carlb_env
         g.seed = cfg.seed;
         g.simOffset = cfg.sim_offset;
         return g;
+    }
+    StageStreams stageStreams() const
+    {
+        StageStreams s{};
+        s.groups = groups;
+        for (int g = 0; g < 8; g++)
+        {
+            s.streams[g] = groupStream[g];
+            s.join[g] = groupJoin[g];
+        }
+        s.fork = evFork;
+        return s;
     }
     ArenaDev arena() const { return ArenaDev{ triV, triAng, cellStart, cellTris, hitWords, cellSph, carReach, cellV }; }
     Outputs outputs() const
@@ -197,8 +213,9 @@ carlb_status launchTicks(carlb_env* e, carlb_action_kind kind, int nTicks)
     p.tileSims = e->tileSims;
     p.compatFlags = e->cfg.compat_flags;
     ECHECK(e, cudaEventRecord(e->ev0, e->stream));
-    const int err = e->staged ? launchTickStaged(p, e->arena(), e->scratch, e->stream)
-                              : launchTick(p, e->arena(), e->stream);
+    const int err = e->staged
+        ? launchTickStaged(p, e->arena(), e->scratch, e->stream, e->stageStreams())
+        : launchTick(p, e->arena(), e->stream);
     if (err) return cudaFail(e, (cudaError_t)err, "tick kernel launch");
     ECHECK(e, cudaEventRecord(e->ev1, e->stream));
     e->tick += nTicks;
@@ -367,6 +384,15 @@ static carlb_status initEnv(carlb_env* p, const carlb_config* cfg)
     }
     if (p->staged)
     {
+        if (const char* g = std::getenv("CARLB_GROUPS")) p->groups = std::max(1, std::min(8, std::atoi(g)));
+        // Slices of fewer than ~4k sims would leave the wide stages too small.
+        p->groups = std::max(1, std::min(p->groups, cfg->n_sim / 4096));
+        for (int g = 0; g < p->groups; g++)
+        {
+            ECHECK(p, cudaStreamCreateWithFlags(&p->groupStream[g], cudaStreamNonBlocking));
+            ECHECK(p, cudaEventCreateWithFlags(&p->groupJoin[g], cudaEventDisableTiming));
+        }
+        ECHECK(p, cudaEventCreateWithFlags(&p->evFork, cudaEventDisableTiming));
         ECHECK(p, allocZero(p, &p->scratch.first, (size_t)p->carStride));
         ECHECK(p, allocZero(p, &p->scratch.cnt, (size_t)p->carStride));
         ECHECK(p, allocZero(p, &p->scratch.ray, (size_t)16 * p->carStride));
@@ -375,10 +401,10 @@ static carlb_status initEnv(carlb_env* p, const carlb_config* cfg)
         ECHECK(p, allocZero(p, &p->scratch.keys, (size_t)4 * p->carStride));
         ECHECK(p, allocZero(p, &p->scratch.heavyBody, (size_t)18 * p->carStride));
         ECHECK(p, allocZero(p, &p->scratch.heavyList, (size_t)p->carStride));
-        ECHECK(p, allocZero(p, &p->scratch.heavyCount, (size_t)1));
+        ECHECK(p, allocZero(p, &p->scratch.heavyCount, (size_t)8));
         ECHECK(p, allocZero(p, &p->scratch.ball, (size_t)15 * p->simStride));
         ECHECK(p, allocZero(p, &p->scratch.ballList, (size_t)p->simStride));
-        ECHECK(p, allocZero(p, &p->scratch.ballCount, (size_t)1));
+        ECHECK(p, allocZero(p, &p->scratch.ballCount, (size_t)8));
     }
     p->actionCapacity = (size_t)p->nCarTotal * 32;
     {
@@ -499,9 +525,17 @@ carlb_status carlb_destroy(carlb_env* e)
     if (!e) return CARLB_OK;
     cudaSetDevice(e->cfg.device);
     if (e->stream) cudaStreamSynchronize(e->stream);
+    for (int g = 0; g < 8; g++)
+        if (e->groupStream[g]) cudaStreamSynchronize(e->groupStream[g]);
     for (void* v : e->allocations) cudaFree(v);
     if (e->ev0) cudaEventDestroy(e->ev0);
     if (e->ev1) cudaEventDestroy(e->ev1);
+    for (int g = 0; g < 8; g++)
+    {
+        if (e->groupJoin[g]) cudaEventDestroy(e->groupJoin[g]);
+        if (e->groupStream[g]) cudaStreamDestroy(e->groupStream[g]);
+    }
+    if (e->evFork) cudaEventDestroy(e->evFork);
     if (e->stream) cudaStreamDestroy(e->stream);
     delete e;
     return CARLB_OK;

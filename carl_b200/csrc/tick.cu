@@ -929,7 +929,8 @@ __global__ void __launch_bounds__(256) tickKernel(TickParams p, ArenaDev arena)
 //   rayCtlKernel   ray finish (arena hit, other cars' boxes, ball), controls
 //   suspKernel     suspension; cars that may touch a plane or the mesh are listed
 //   contactKernel  plane + mesh manifold and car-arena solve of the listed cars
-//   carCarKernel   ball prelude (moving balls are listed), car-car pairs per sim
+//   ballPrepKernel ball prelude (moving balls are listed)
+//   carCarKernel   car-car pairs per sim
 //   ballKernel     ball arena contacts, one warp per listed ball
 //   finishKernel   ball vs cars + integration + goal, car integration + finish, boost pads
 // =========================================================================================
@@ -941,6 +942,7 @@ constexpr int SOLVE_BLOCK = 128;  // cars per suspKernel / contactKernel CTA
 constexpr int CC_BLOCK = 128;     // sims per carCarKernel CTA
 constexpr int BALL_WARPS = 4;     // sims (warps) per ballKernel CTA
 constexpr int FIN_THREADS = 256;  // threads per finishKernel CTA
+constexpr int STAGE_MAX_GROUPS = 8;  // sim slices stepped on separate streams
 
 using CarSoa = Soa<int>;  // int indexing: NCW * carStride < 2^31 is checked at launch
 
@@ -1042,41 +1044,30 @@ __global__ void __launch_bounds__(CAND_BLOCK) flatKernel(TickParams p, ArenaDev 
     }
     __syncthreads();
 
-    // Flattened (car, candidate) work: wheel rays and SAT.
+    // Flattened (car, candidate) work: wheel rays and SAT.  Two items per thread
+    // per round, their loads issued together, to keep more of them in flight.
     const int total = preS[here];
-    for (int it = tid; it < total; it += B)
-    {
-        int c;
-        if (it < CAND_MAP_CAP)
+    auto carOf = [&](int it) -> int {
+        if (it < CAND_MAP_CAP) return mapS[it];
+        int lo = 0, hi = here - 1;
+        while (lo < hi)
         {
-            c = mapS[it];
+            const int mid = (lo + hi + 1) >> 1;
+            if (preS[mid] <= it) lo = mid;
+            else hi = mid - 1;
         }
-        else
-        {
-            int lo = 0, hi = here - 1;
-            while (lo < hi)
-            {
-                const int mid = (lo + hi + 1) >> 1;
-                if (preS[mid] <= it) lo = mid;
-                else hi = mid - 1;
-            }
-            c = lo;
-        }
-        const int k = it - preS[c];
-        const int e = firstS[c] + k;
-        const V3 cc = { poseS[0 * B + c], poseS[1 * B + c], poseS[2 * B + c] };
-        {
-            const float4 sph = __ldg(&arena.cellSph[e]);
-            const float dx = sph.x - cc.x, dy = sph.y - cc.y, dz = sph.z - cc.z;
-            const float rr = sph.w + arena.carReach;
-            if (dx * dx + dy * dy + dz * dz > rr * rr) continue;
-        }
-        const float4 q0 = __ldg(&arena.cellV[3 * e]);
-        const float4 q1 = __ldg(&arena.cellV[3 * e + 1]);
-        const float4 q2 = __ldg(&arena.cellV[3 * e + 2]);
+        return lo;
+    };
+    auto inReach = [&](int c, float4 sph) -> bool {
+        // Triangles out of reach of the box and the wheel rays cannot produce a
+        // ray hit or a SAT overlap.
+        const float dx = sph.x - poseS[0 * B + c], dy = sph.y - poseS[1 * B + c], dz = sph.z - poseS[2 * B + c];
+        const float rr = sph.w + arena.carReach;
+        return !(dx * dx + dy * dy + dz * dz > rr * rr);
+    };
+    auto process = [&](int c, int k, float4 q0, float4 q1, float4 q2) {
         const V3 v0 = { q0.x, q0.y, q0.z }, v1 = { q1.x, q1.y, q1.z }, v2 = { q2.x, q2.y, q2.z };
         const int flags = __float_as_int(q0.w);
-
         const V3 dir = { rsS[12 * B + c], rsS[13 * B + c], rsS[14 * B + c] };
         const V3 e1 = v1 - v0;
         const V3 e2 = v2 - v0;
@@ -1102,10 +1093,41 @@ __global__ void __launch_bounds__(CAND_BLOCK) flatKernel(TickParams p, ArenaDev 
         }
         if (!(flags & 1))
         {
+            const V3 cc = { poseS[0 * B + c], poseS[1 * B + c], poseS[2 * B + c] };
             const Q4 cr = { poseS[3 * B + c], poseS[4 * B + c], poseS[5 * B + c], poseS[6 * B + c] };
             const LocalTri lt = localTriangle(cc, cr, v0, v1, v2);
             if (carTriSat(lt).overlap) atomicOr(&hitS[(k >> 5) * B + c], 1u << (k & 31));
         }
+    };
+    for (int itA = tid; itA < total; itA += 2 * B)
+    {
+        const int itB = itA + B;
+        const bool hasB = itB < total;
+        const int cA = carOf(itA);
+        const int cB = hasB ? carOf(itB) : cA;
+        const int kA = itA - preS[cA];
+        const int kB = hasB ? itB - preS[cB] : kA;
+        const int eA = firstS[cA] + kA;
+        const int eB = firstS[cB] + kB;
+        const float4 sA = __ldg(&arena.cellSph[eA]);
+        const float4 sB = __ldg(&arena.cellSph[eB]);
+        const bool keepA = inReach(cA, sA);
+        const bool keepB = hasB && inReach(cB, sB);
+        float4 a0, a1, a2, b0, b1, b2;
+        if (keepA)
+        {
+            a0 = __ldg(&arena.cellV[3 * eA]);
+            a1 = __ldg(&arena.cellV[3 * eA + 1]);
+            a2 = __ldg(&arena.cellV[3 * eA + 2]);
+        }
+        if (keepB)
+        {
+            b0 = __ldg(&arena.cellV[3 * eB]);
+            b1 = __ldg(&arena.cellV[3 * eB + 1]);
+            b2 = __ldg(&arena.cellV[3 * eB + 2]);
+        }
+        if (keepA) process(cA, kA, a0, a1, a2);
+        if (keepB) process(cB, kB, b0, b1, b2);
     }
     __syncthreads();
     if (!valid) return;
@@ -1419,7 +1441,7 @@ __global__ void __launch_bounds__(SOLVE_BLOCK) contactKernel(TickParams p, Arena
     }
 }
 
-__global__ void __launch_bounds__(CC_BLOCK) carCarKernel(TickParams p, StageScratch x, int t)
+__global__ void __launch_bounds__(CC_BLOCK) carCarKernel(TickParams p, int t)
 {
     __shared__ int activeS[CC_BLOCK];
     __shared__ int nActive;
@@ -1434,15 +1456,6 @@ __global__ void __launch_bounds__(CC_BLOCK) carCarKernel(TickParams p, StageScra
     __syncthreads();
     if (s < p.nSim)
     {
-        // Ball stage prelude (reads only the ball, which car-car leaves alone):
-        // hand-over values for every sim, and the list of moving balls, the only
-        // ones with arena work.
-        const CarSoa sims{ p.sim, (int)p.simStride };
-        const BallPre bp = ballPre(sims, s);
-        const V3 out[5] = { bp.exportedPos, bp.posBT, bp.preSolveBT, v3zero(), bp.velNoExt };
-        storeBallScratch(x.ball, (int)p.simStride, s, out, 0, 5);
-        if (!bp.sleeping) x.ballList[atomicAdd(x.ballCount, 1)] = s;
-
         const int sb = s * nCars;
         bool gate = false;
         for (int a = 0; a < nCars - 1 && !gate; a++)
@@ -1463,6 +1476,20 @@ __global__ void __launch_bounds__(CC_BLOCK) carCarKernel(TickParams p, StageScra
             const int kept = solveCarCarPair(sc, b, a);
             if (lastTick && p.diagSim && pair < DIAG_SIM_WORDS) p.diagSim[pair * p.simStride + sIdx] = kept;
         }
+}
+
+// Ball stage prelude, one thread per sim: hand-over values for every sim and the
+// list of moving balls (the only ones with arena work).  It reads only the ball,
+// which no car stage of the tick writes before the finish kernel.
+__global__ void __launch_bounds__(256) ballPrepKernel(TickParams p, StageScratch x)
+{
+    const int s = blockIdx.x * 256 + threadIdx.x;
+    if (s >= p.nSim) return;
+    const CarSoa sims{ p.sim, (int)p.simStride };
+    const BallPre bp = ballPre(sims, s);
+    const V3 out[5] = { bp.exportedPos, bp.posBT, bp.preSolveBT, v3zero(), bp.velNoExt };
+    storeBallScratch(x.ball, (int)p.simStride, s, out, 0, 5);
+    if (!bp.sleeping) x.ballList[atomicAdd(x.ballCount, 1)] = s;
 }
 
 __global__ void __launch_bounds__(BALL_WARPS * 32) ballKernel(TickParams p, ArenaDev arena, StageScratch x, int t)
@@ -1600,13 +1627,13 @@ size_t stageCandSmemBytes(int hitWords)
     return bytes + 8 * 4 * (size_t)B + CAND_MAP_CAP;
 }
 
-int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch& x, void* stream)
+int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch& x, void* stream,
+                     const StageStreams& aux)
 {
     if (p.nTicks <= 0 || p.nSim <= 0) return 0;
     if ((long long)NCW * p.carStride >= (1LL << 31) || (long long)NSW * p.simStride >= (1LL << 31))
         return (int)cudaErrorInvalidValue;
     cudaStream_t st = (cudaStream_t)stream;
-    const int n = p.nSim * p.nCars;
     const size_t candSmem = stageCandSmemBytes(a.hitWords);
     static bool configured[64] = {};
     int dev = 0;
@@ -1619,21 +1646,82 @@ int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch&
         if (dev >= 0 && dev < 64) configured[dev] = true;
     }
     if (candSmem > 64 * 1024) return (int)cudaErrorInvalidValue;
-    const int simsPerFin = FIN_THREADS / p.nCars;
-    // Warps loop over the moving balls; enough CTAs for a few per SM, never more than the sims.
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int ballBlocks = std::max(1, std::min((p.nSim + BALL_WARPS - 1) / BALL_WARPS, sms * 8));
-    const int contactBlocks = std::max(1, std::min((n + SOLVE_BLOCK - 1) / SOLVE_BLOCK, sms * 4));
-    for (int t = 0; t < p.nTicks; t++)
+
+    // Sims are independent, so the env's sims are split into `groups` contiguous
+    // slices, each stepped on its own stream: while one slice runs a stage that
+    // leaves the GPU half idle (the contact solve of a few cars, the ball arena
+    // stage), another slice's wide stages fill it.  A slice is the env itself seen
+    // through shifted base pointers (every array is word-major with the env's
+    // strides), with its own work-list counters.
+    const int groups = std::max(1, std::min(aux.groups, STAGE_MAX_GROUPS));
+    cudaError_t err = cudaEventRecord((cudaEvent_t)aux.fork, st);
+    if (err != cudaSuccess) return (int)err;
+    TickParams gp[STAGE_MAX_GROUPS];
+    StageScratch gx[STAGE_MAX_GROUPS];
+    cudaStream_t gs[STAGE_MAX_GROUPS];
+    int nG = 0;
+    const int per = (p.nSim + groups - 1) / groups;
+    for (int g = 0; g < groups; g++)
     {
-        flatKernel<<<(n + CAND_BLOCK - 1) / CAND_BLOCK, CAND_BLOCK, candSmem, st>>>(p, a, x, t);
-        rayCtlKernel<<<(n + RAY_BLOCK - 1) / RAY_BLOCK, RAY_BLOCK, 0, st>>>(p, a, x, t);
-        suspKernel<<<(n + SOLVE_BLOCK - 1) / SOLVE_BLOCK, SOLVE_BLOCK, 0, st>>>(p, a, x, t);
-        contactKernel<<<contactBlocks, SOLVE_BLOCK, 0, st>>>(p, a, x, t);
-        carCarKernel<<<(p.nSim + CC_BLOCK - 1) / CC_BLOCK, CC_BLOCK, 0, st>>>(p, x, t);
-        ballKernel<<<ballBlocks, BALL_WARPS * 32, 0, st>>>(p, a, x, t);
-        finishKernel<<<(p.nSim + simsPerFin - 1) / simsPerFin, FIN_THREADS, 0, st>>>(p, x, t, simsPerFin);
+        const int s0 = g * per;
+        const int ns = std::min(per, p.nSim - s0);
+        if (ns <= 0) break;
+        const long long c0 = (long long)s0 * p.nCars;
+        TickParams q = p;
+        q.car = p.car + c0;
+        q.sim = p.sim + s0;
+        q.carOut = p.carOut + c0;
+        q.diagCar = p.diagCar ? p.diagCar + c0 : nullptr;
+        q.diagSim = p.diagSim ? p.diagSim + s0 : nullptr;
+        const size_t rowBytes = p.actionKind == ACT_DIRECT ? 32 : 28;
+        q.actions = static_cast<const char*>(p.actions) + c0 * rowBytes;
+        q.globalCarBase = p.globalCarBase + c0;
+        q.nSim = ns;
+        StageScratch y = x;
+        y.first = x.first + c0;
+        y.cnt = x.cnt + c0;
+        y.ray = x.ray + c0;
+        y.hits = x.hits + c0;
+        y.wheelBits = x.wheelBits + c0;
+        y.keys = x.keys + c0;
+        y.heavyBody = x.heavyBody + c0;
+        y.heavyList = x.heavyList + c0;
+        y.heavyCount = x.heavyCount + g;
+        y.ball = x.ball + s0;
+        y.ballList = x.ballList + s0;
+        y.ballCount = x.ballCount + g;
+        gp[nG] = q;
+        gx[nG] = y;
+        gs[nG] = groups == 1 ? st : (cudaStream_t)aux.streams[g];
+        if (gs[nG] != st && (err = cudaStreamWaitEvent(gs[nG], (cudaEvent_t)aux.fork, 0)) != cudaSuccess) return (int)err;
+        nG++;
+    }
+    for (int t = 0; t < p.nTicks; t++)
+        for (int g = 0; g < nG; g++)
+        {
+            const TickParams& q = gp[g];
+            const StageScratch& y = gx[g];
+            cudaStream_t sq = gs[g];
+            const int n = q.nSim * q.nCars;
+            const int simsPerFin = FIN_THREADS / q.nCars;
+            const int ballBlocks = std::max(1, std::min((q.nSim + BALL_WARPS - 1) / BALL_WARPS, sms * 8 / nG));
+            const int contactBlocks = std::max(1, std::min((n + SOLVE_BLOCK - 1) / SOLVE_BLOCK, sms * 4 / nG));
+            ballPrepKernel<<<(q.nSim + 255) / 256, 256, 0, sq>>>(q, y);
+            flatKernel<<<(n + CAND_BLOCK - 1) / CAND_BLOCK, CAND_BLOCK, candSmem, sq>>>(q, a, y, t);
+            rayCtlKernel<<<(n + RAY_BLOCK - 1) / RAY_BLOCK, RAY_BLOCK, 0, sq>>>(q, a, y, t);
+            suspKernel<<<(n + SOLVE_BLOCK - 1) / SOLVE_BLOCK, SOLVE_BLOCK, 0, sq>>>(q, a, y, t);
+            contactKernel<<<contactBlocks, SOLVE_BLOCK, 0, sq>>>(q, a, y, t);
+            carCarKernel<<<(q.nSim + CC_BLOCK - 1) / CC_BLOCK, CC_BLOCK, 0, sq>>>(q, t);
+            ballKernel<<<ballBlocks, BALL_WARPS * 32, 0, sq>>>(q, a, y, t);
+            finishKernel<<<(q.nSim + simsPerFin - 1) / simsPerFin, FIN_THREADS, 0, sq>>>(q, y, t, simsPerFin);
+        }
+    for (int g = 0; g < nG; g++)
+    {
+        if (gs[g] == st) continue;
+        if ((err = cudaEventRecord((cudaEvent_t)aux.join[g], gs[g])) != cudaSuccess) return (int)err;
+        if ((err = cudaStreamWaitEvent(st, (cudaEvent_t)aux.join[g], 0)) != cudaSuccess) return (int)err;
     }
     return (int)cudaGetLastError();
 }

@@ -52,10 +52,10 @@ struct StageScratch
     unsigned long long* keys;  // [4][carStride] wheel ray minimum (distance bits, candidate)
     float* heavyBody;       // [18][carStride] velocities after the suspension of listed cars
     int* heavyList;         // [carStride] cars with possible plane / mesh contacts, this tick
-    int* heavyCount;        // [1] entries of heavyList; zero between ticks
+    int* heavyCount;        // [slices] entries of each slice's heavyList; zero between ticks
     float* ball;            // [15][simStride] ball stage hand-over values
     int* ballList;          // [simStride] sims whose ball is moving (arena work), this tick
-    int* ballCount;         // [1] entries of ballList; zero between ticks
+    int* ballCount;         // [slices] entries of each slice's ballList; zero between ticks
 };
 
 struct Tables;
@@ -69,7 +69,18 @@ int tickThreads(int tileSims, int nCars);
 // Launches ceil(nSim / tileSims) CTAs on `stream`.
 int launchTick(const TickParams& p, const ArenaDev& a, void* stream);
 
+// Streams and events of the staged path (cudaStream_t / cudaEvent_t): the sims
+// are split into `groups` slices stepped concurrently on streams[0..groups).
+struct StageStreams
+{
+    int groups;
+    void* streams[8];
+    void* join[8];    // event per slice: its last kernel
+    void* fork;       // event: work queued on the env stream before the launch
+};
+
 // The same ticks as a sequence of stage kernels over the state in global memory.
-int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch& x, void* stream);
+int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch& x, void* stream,
+                     const StageStreams& aux);
 
 }  // namespace cb

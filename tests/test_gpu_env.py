@@ -255,3 +255,22 @@ def test_stream_is_the_envs_own():
     ext.synchronize()
     assert float(y.sum()) == 2048.0
     env.close()
+
+
+def test_sim_slices_equal_single_slice(monkeypatch):
+    """The staged tick steps large envs as several sim slices on separate
+    streams; the result is bit-identical to stepping them as one slice."""
+    t = torch()
+    n_sim, nb, no = 16384, 2, 2
+    snaps = []
+    for groups in ("1", "4"):
+        monkeypatch.setenv("CARLB_GROUPS", groups)
+        env = capi.Env(n_sim, nb, no, 3)
+        workloads.mixed_state(env, 5)
+        rng = np.random.default_rng(6)
+        for _ in range(3):
+            env.ticks(capi.ACTIONS_DIRECT, t.from_numpy(workloads.controls(rng, n_sim * (nb + no)).view(np.int32)).cuda(), 8)
+        snaps.append(env.snapshot())
+        env.close()
+    for name in snaps[0]:
+        assert (snaps[0][name] == snaps[1][name]).all(), name
