@@ -20,7 +20,9 @@ per-GPU work is fixed (weak scaling) and there is no collective in the tick.
 Timed region: barrier + synchronize, K steps, synchronize + barrier.  Each
 step's device time is taken with CUDA events on the env stream; between timed
 steps a 256 MiB buffer is written to flush the 126 MB L2 (outside the events).
-The roofline uses the tick kernel's own event time, read back per launch.
+The roofline uses the event-timed duration of the dominant stage kernel (CUDA
+events around each stage kernel of the first sim slice, last tick of each step),
+and a second figure covers the whole tick.
 """
 
 from __future__ import annotations
@@ -42,10 +44,26 @@ import numpy as np  # noqa: E402
 
 TICKS_PER_STEP = 8
 FLUSH_BYTES = 256 << 20
-# Byte model CARLB-v1: persistent tick state read once and written once per
-# tick, packed fp32 (vec3 12 B, quat 16 B, ints 4 B), plus the actions read.
+# Byte model CARLB-v1 of a whole tick: persistent tick state read once and
+# written once per tick, packed fp32 (vec3 12 B, quat 16 B, ints 4 B), plus the
+# actions read.
 BYTES_PER_CAR_TICK = 620
 BYTES_PER_SIM_TICK = 504
+# Algorithmic bytes of single stage kernels, per car and per sim of one tick:
+# the words the stage must read and write (arena tables are L2-resident and
+# excluded).  flat: pose in (pos, vel, ang, cen, rot: 16 words), candidate
+# list start, count, SAT hit mask (9 words) and ray keys (8 words) out, episode
+# tick read-modify-write per sim.  rayCtl: pose, keys, controls state in
+# (74 words), rays, wheel bits and controls state out (62 words), ball position
+# per sim.  susp: hits, rays, body, suspension, friction and manifold state in
+# (70 words), suspension state, friction and velocities out (33 words).
+# ballPrep: ball state in (22 words), hand-over values out (15 words).
+STAGE_BYTES = {
+    "flat": (140, 8),
+    "rayCtl": (544, 12),
+    "susp": (412, 0),
+    "ballPrep": (0, 148),
+}
 METRIC = "agent-steps/sec at 3v3 n_sim=32768"
 UNIT = "agent-steps/s"
 
@@ -141,15 +159,29 @@ def control_pool(n_cars_total: int, count: int, seed: int):
     return [workloads.controls(rng, n_cars_total) for _ in range(count)]
 
 
-def traffic_per_launch() -> float | None:
-    """DRAM bytes per tick-kernel launch at this workload, from the committed ncu summary."""
-    path = ROOT / "profiles" / "tick_kernel_3v3_32768.md"
+def traffic_per_launch(stage: str) -> float | None:
+    """DRAM bytes per launch of a stage kernel at this workload, from the
+    committed ncu summary of the staged tick (None when not captured)."""
+    path = ROOT / "profiles" / "staged_tick_3v3_32768.md"
     if not path.exists():
         return None
+    key = f"traffic_bytes_per_launch[{stage}]:"
     for line in path.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_launch:"):
+        if line.startswith(key):
             return float(line.split(":", 1)[1].split()[0])
     return None
+
+
+def world_groups(args) -> int:
+    """Sim slices the library steps concurrently (CARLB_GROUPS, default 2; one
+    slice per 4096 sims at most)."""
+    g = int(os.environ.get("CARLB_GROUPS", "2"))
+    return max(1, min(8, g, args.n_sim // 4096))
+
+
+def launches_per_step(groups: int) -> int:
+    """Kernels of the library launched per step: 8 stage kernels per tick and slice."""
+    return 8 * TICKS_PER_STEP * groups
 
 
 def measured_hbm_peak() -> tuple[float, str]:
@@ -291,6 +323,8 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     kernel_ms = []
+    stage_ms: dict[str, list[float]] = {}
+    env.set_stage_timing(True)
     sampler = ClockSampler(device)
     sampler.start()
     barrier()
@@ -304,6 +338,8 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         ends[i].record(stream)
         env.synchronize()
         kernel_ms.append(env.last_tick_ms())
+        for name, ms in env.stage_times().items():
+            stage_ms.setdefault(name, []).append(ms)
     torch.cuda.synchronize()
     barrier()
     wall = time.perf_counter() - wall0
@@ -315,6 +351,8 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     step_ms, kern_ms = float(t[0]), float(t[1])
+    env.set_stage_timing(False)
+    stage_avg = {k: sum(v) / len(v) for k, v in stage_ms.items()}
 
     agent_ticks_rank = n_total_cars * TICKS_PER_STEP * args.steps
     value = agent_ticks_rank * world / (step_ms / 1e3)
@@ -350,16 +388,25 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         env.close()
         return
 
-    # ---- roofline of the fused tick kernel ----
+    # ---- roofline of the dominant stage kernel, and of the whole tick ----
     peak, peak_kind = measured_hbm_peak()
-    bpat = bytes_per_agent_tick(n_cars)
-    launch_ms = kern_ms / args.steps
-    alg_bytes = bpat * n_total_cars * TICKS_PER_STEP
-    achieved = alg_bytes / (launch_ms / 1e3) / 1e9
+    modelled = {k: v for k, v in stage_avg.items() if k in STAGE_BYTES}
+    dom = max(modelled, key=modelled.get)
+    per_car, per_sim = STAGE_BYTES[dom]
+    dom_bytes = per_car * n_total_cars + per_sim * args.n_sim
+    dom_ms = stage_avg[dom]
+    achieved = dom_bytes / (dom_ms / 1e3) / 1e9
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "traffic": traffic_per_launch(), "peak_kind": peak_kind, "kernel": "tickKernel",
-                "launch_ms": launch_ms, "bytes_per_agent_tick": bpat,
-                "algorithmic_bytes_per_launch": alg_bytes}
+                "traffic": traffic_per_launch(dom), "peak_kind": peak_kind, "kernel": dom + "Kernel",
+                "launch_ms": dom_ms, "algorithmic_bytes_per_launch": dom_bytes,
+                "stage_ms": {k: round(v, 4) for k, v in stage_avg.items()},
+                "largest_stage": max(stage_avg, key=stage_avg.get)}
+    bpat = bytes_per_agent_tick(n_cars)
+    tick_ms = kern_ms / args.steps / TICKS_PER_STEP
+    tick_achieved = bpat * n_total_cars / (tick_ms / 1e3) / 1e9
+    roofline_tick = {"bound": "hbm", "achieved": tick_achieved, "peak": peak, "unit": "GB/s",
+                     "frac": tick_achieved / peak, "model": "CARLB-v1", "bytes_per_agent_tick": bpat,
+                     "tick_ms": tick_ms}
 
     cpu = None
     if snap0 is not None:
@@ -385,7 +432,8 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
                    "ticks_per_step": TICKS_PER_STEP, "sims_total": args.n_sim * world,
                    "parallelism": f"sim-sharded x{world}", "l2": "256 MiB buffer written between timed steps",
                    "wall_s": wall},
-        "clocks": clocks, "e2e": e2e, "gpu_launches": args.steps, "roofline": roofline, "cpu_baseline": cpu,
+        "clocks": clocks, "e2e": e2e, "gpu_launches": args.steps * launches_per_step(world_groups(args)),
+        "roofline": roofline, "roofline_tick": roofline_tick, "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)
     env.close()

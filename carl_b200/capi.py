@@ -116,6 +116,8 @@ def load() -> ctypes.CDLL:
     lib.carlb_write_field.argtypes = [vp, i32, vp]
     lib.carlb_set_diagnostics.argtypes = [vp, i32]
     lib.carlb_last_tick_ms.argtypes = [vp, ctypes.POINTER(ctypes.c_float)]
+    lib.carlb_set_stage_timing.argtypes = [vp, i32]
+    lib.carlb_stage_times.argtypes = [vp, ctypes.POINTER(ctypes.c_float), i32, ctypes.POINTER(i32)]
     _lib = lib
     return lib
 
@@ -288,6 +290,18 @@ class Env:
         ms = ctypes.c_float()
         self._check(self._lib.carlb_last_tick_ms(self._h, ctypes.byref(ms)))
         return ms.value
+
+    STAGES = ["ballPrep", "flat", "rayCtl", "susp", "contact", "carCar", "ball", "finish"]
+
+    def set_stage_timing(self, enabled: bool) -> None:
+        self._check(self._lib.carlb_set_stage_timing(self._h, int(enabled)))
+
+    def stage_times(self) -> dict[str, float]:
+        """Milliseconds per stage kernel of the last timed tick (staged path)."""
+        ms = (ctypes.c_float * 16)()
+        n = ctypes.c_int32()
+        self._check(self._lib.carlb_stage_times(self._h, ms, 16, ctypes.byref(n)))
+        return {self.STAGES[k]: ms[k] for k in range(n.value)}
 
     # ---- snapshot ----
     def field_shape(self, name: str) -> tuple[int, int]:

@@ -93,6 +93,9 @@ struct carlb_env
     cudaStream_t groupStream[8] = {};
     cudaEvent_t groupJoin[8] = {};
     cudaEvent_t evFork = nullptr;
+    bool stageTiming = false;
+    bool stageTimed = false;  // the last launch recorded stage events
+    cudaEvent_t stageEv[STAGE_KERNELS + 1] = {};
 
     float *obs = nullptr, *tobs = nullptr, *packed = nullptr, *tpacked = nullptr, *rewards = nullptr;
     uint8_t *dones = nullptr, *overtime = nullptr, *tovertime = nullptr;
@@ -136,6 +139,7 @@ struct carlb_env
             s.join[g] = groupJoin[g];
         }
         s.fork = evFork;
+        for (int k = 0; k <= STAGE_KERNELS; k++) s.stageEvents[k] = stageTiming ? stageEv[k] : nullptr;
         return s;
     }
     ArenaDev arena() const { return ArenaDev{ triV, triAng, cellStart, cellTris, hitWords, cellSph, carReach, cellV }; }
@@ -217,6 +221,7 @@ carlb_status launchTicks(carlb_env* e, carlb_action_kind kind, int nTicks)
         ? launchTickStaged(p, e->arena(), e->scratch, e->stream, e->stageStreams())
         : launchTick(p, e->arena(), e->stream);
     if (err) return cudaFail(e, (cudaError_t)err, "tick kernel launch");
+    e->stageTimed = e->staged && e->stageTiming && nTicks > 0;
     ECHECK(e, cudaEventRecord(e->ev1, e->stream));
     e->tick += nTicks;
     return CARLB_OK;
@@ -400,8 +405,8 @@ static carlb_status initEnv(carlb_env* p, const carlb_config* cfg)
         ECHECK(p, allocZero(p, &p->scratch.wheelBits, (size_t)p->carStride));
         ECHECK(p, allocZero(p, &p->scratch.keys, (size_t)4 * p->carStride));
         ECHECK(p, allocZero(p, &p->scratch.heavyBody, (size_t)18 * p->carStride));
-        ECHECK(p, allocZero(p, &p->scratch.heavyList, (size_t)p->carStride));
-        ECHECK(p, allocZero(p, &p->scratch.heavyCount, (size_t)8));
+        ECHECK(p, allocZero(p, &p->scratch.heavyList, (size_t)HEAVY_CLASSES * p->carStride));
+        ECHECK(p, allocZero(p, &p->scratch.heavyCount, (size_t)8 * HEAVY_CLASSES));
         ECHECK(p, allocZero(p, &p->scratch.ball, (size_t)15 * p->simStride));
         ECHECK(p, allocZero(p, &p->scratch.ballList, (size_t)p->simStride));
         ECHECK(p, allocZero(p, &p->scratch.ballCount, (size_t)8));
@@ -536,6 +541,8 @@ carlb_status carlb_destroy(carlb_env* e)
         if (e->groupStream[g]) cudaStreamDestroy(e->groupStream[g]);
     }
     if (e->evFork) cudaEventDestroy(e->evFork);
+    for (int k = 0; k <= STAGE_KERNELS; k++)
+        if (e->stageEv[k]) cudaEventDestroy(e->stageEv[k]);
     if (e->stream) cudaStreamDestroy(e->stream);
     delete e;
     return CARLB_OK;
@@ -823,6 +830,32 @@ carlb_status carlb_write_field(carlb_env* e, carlb_field field, const void* in)
         for (long long r = 0; r < m.rows; r++) col[r] = src[r * m.width + k];
         uint32_t* dst = static_cast<uint32_t*>(m.base) + (long long)(m.word + k) * m.stride;
         ECHECK(e, cudaMemcpy(dst, col.data(), (size_t)m.rows * 4, cudaMemcpyHostToDevice));
+    }
+    return CARLB_OK;
+}
+
+carlb_status carlb_set_stage_timing(carlb_env* e, int32_t enabled)
+{
+    if (!e) return fail(nullptr, CARLB_ERR_VALUE, "env is null");
+    if (!e->staged) return fail(e, CARLB_ERR_STATE, "stage timing needs the staged tick path");
+    ECHECK(e, cudaSetDevice(e->cfg.device));
+    for (int k = 0; k <= STAGE_KERNELS && enabled; k++)
+        if (!e->stageEv[k]) ECHECK(e, cudaEventCreate(&e->stageEv[k]));
+    e->stageTiming = enabled != 0;
+    e->stageTimed = false;
+    return CARLB_OK;
+}
+
+carlb_status carlb_stage_times(carlb_env* e, float* ms, int32_t capacity, int32_t* count)
+{
+    if (!e || !count) return fail(e, CARLB_ERR_VALUE, "env or count is null");
+    *count = 0;
+    if (!e->stageTimed) return fail(e, CARLB_ERR_STATE, "no timed launch since stage timing was enabled");
+    ECHECK(e, cudaEventSynchronize(e->stageEv[STAGE_KERNELS]));
+    for (int k = 0; k < STAGE_KERNELS && k < capacity; k++)
+    {
+        ECHECK(e, cudaEventElapsedTime(&ms[k], e->stageEv[k], e->stageEv[k + 1]));
+        *count = k + 1;
     }
     return CARLB_OK;
 }

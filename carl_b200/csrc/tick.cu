@@ -1356,7 +1356,10 @@ __global__ void __launch_bounds__(SOLVE_BLOCK) suspKernel(TickParams p, ArenaDev
             x.heavyBody[(long long)(3 * k + 1) * p.carStride + i] = hv[k].y;
             x.heavyBody[(long long)(3 * k + 2) * p.carStride + i] = hv[k].z;
         }
-        x.heavyList[atomicAdd(x.heavyCount, 1)] = i;
+        // Two lists: cars with SAT hits (a warp each in the contact kernel, lanes
+        // over the hits) and cars with plane contacts only (a thread each).
+        const int cls = anyHit ? 1 : 0;
+        x.heavyList[(long long)cls * p.carStride + atomicAdd(&x.heavyCount[cls], 1)] = i;
         return;
     }
     cars.n(C_MAN_COUNT, i) = 0;
@@ -1365,79 +1368,155 @@ __global__ void __launch_bounds__(SOLVE_BLOCK) suspKernel(TickParams p, ArenaDev
     cars.setv(C_ANG, i, body.ang + body.extAng + body.deltaAng);
 }
 
-__global__ void __launch_bounds__(SOLVE_BLOCK) contactKernel(TickParams p, ArenaDev arena, StageScratch x, int t)
+// Velocities after the suspension of a listed car (from suspKernel).
+__device__ __forceinline__ Body loadHeavyBody(const CarSoa& cars, const StageScratch& x, long long stride, int i)
 {
-    const int count = *x.heavyCount;
-    const CarSoa cars{ p.car, (int)p.carStride };
-    const int HW = arena.hitWords;
-    for (int j = blockIdx.x * SOLVE_BLOCK + threadIdx.x; j < count; j += gridDim.x * SOLVE_BLOCK)
+    Body body = loadCarBody(cars, i);
+    V3 hv[6];
+    #pragma unroll
+    for (int k = 0; k < 6; k++)
+        hv[k] = V3{ x.heavyBody[(3 * k) * stride + i], x.heavyBody[(3 * k + 1) * stride + i],
+                    x.heavyBody[(3 * k + 2) * stride + i] };
+    body.vel = hv[0];
+    body.ang = hv[1];
+    body.extVel = hv[2];
+    body.extAng = hv[3];
+    body.deltaVel = hv[4];
+    body.deltaAng = hv[5];
+    return body;
+}
+
+// Manifold solve and final store of a listed car (src/Physics/CarArena/Solve.cuh order).
+__device__ __forceinline__ void finishContactCar(const CarSoa& cars, int i, Body& body, MPoint* pts, int cnt)
+{
+    if (cnt > 0)
     {
-        const int i = x.heavyList[j];
-        Body body = loadCarBody(cars, i);
-        V3 hv[6];
-        #pragma unroll
-        for (int k = 0; k < 6; k++)
-            hv[k] = V3{ x.heavyBody[(long long)(3 * k) * p.carStride + i], x.heavyBody[(long long)(3 * k + 1) * p.carStride + i],
-                        x.heavyBody[(long long)(3 * k + 2) * p.carStride + i] };
-        body.vel = hv[0];
-        body.ang = hv[1];
-        body.extVel = hv[2];
-        body.extAng = hv[3];
-        body.deltaVel = hv[4];
-        body.deltaAng = hv[5];
+        solveCarManifold(body, pts, cnt);
+        integrateSplitCorrection(body);
+    }
+    cars.n(C_MAN_COUNT, i) = cnt;
+    cars.setv(C_MAN_N0, i, cnt > 0 ? pts[0].worldNormal : v3zero());
+    body.vel = body.vel + body.extVel + body.deltaVel;
+    body.ang = body.ang + body.extAng + body.deltaAng;
+    storeCarBody(cars, i, body);
+}
+
+// Plane and mesh contacts and the car-arena solve of the listed cars.  The first
+// `planeBlocks` CTAs take the plane-only cars, a thread each; the others take the
+// cars with SAT hits, a warp each: lane r builds the contacts of the r-th hit (in
+// candidate order) and keeps its deepest (first on ties), and a warp reduction in
+// hit order then picks exactly the contact the sequential loop over hits keeps.
+__global__ void __launch_bounds__(SOLVE_BLOCK) contactKernel(TickParams p, ArenaDev arena, StageScratch x, int t,
+                                                            int planeBlocks)
+{
+    const CarSoa cars{ p.car, (int)p.carStride };
+    const long long stride = p.carStride;
+    if ((int)blockIdx.x < planeBlocks)
+    {
+        const int count = x.heavyCount[0];
+        for (int j = blockIdx.x * SOLVE_BLOCK + threadIdx.x; j < count; j += planeBlocks * SOLVE_BLOCK)
+        {
+            const int i = x.heavyList[j];
+            Body body = loadHeavyBody(cars, x, stride, i);
+            MPoint pts[MAX_CAR_MANIFOLD_POINTS];
+            const int cnt = planeManifold(body.cen, body.rot, pts);
+            finishContactCar(cars, i, body, pts, cnt);
+        }
+        return;
+    }
+    const int HW = arena.hitWords;
+    const int lane = threadIdx.x & 31;
+    const int warpsPer = SOLVE_BLOCK / 32;
+    const int count = x.heavyCount[1];
+    const int* list = x.heavyList + stride;
+    for (int j = ((int)blockIdx.x - planeBlocks) * warpsPer + (threadIdx.x >> 5); j < count;
+         j += ((int)gridDim.x - planeBlocks) * warpsPer)
+    {
+        const int i = list[j];
+        Body body = loadHeavyBody(cars, x, stride, i);
         const V3 cen = body.cen;
         const Q4 rot = body.rot;
         const int cellFirst = x.first[i];
-
         MPoint pts[MAX_CAR_MANIFOLD_POINTS];
         int cnt = planeManifold(cen, rot, pts);
         const int planeCount = cnt;
+
+        // Entry of this lane's hit: the lane-th set bit over the hit words (the
+        // first MAX_CAR_TRI_PAIRS hits are used, as in the reference's slots).
+        int myEntry = -1;
+        {
+            int base = 0;
+            for (int h = 0; h < HW && myEntry < 0; h++)
+            {
+                unsigned m = x.hits[h * stride + i];
+                const int c = __popc(m);
+                if (lane < base + c)
+                {
+                    for (int r = base; r < lane; r++) m &= m - 1;
+                    myEntry = cellFirst + h * 32 + __ffs(m) - 1;
+                }
+                base += c;
+            }
+            if (lane >= MAX_CAR_TRI_PAIRS) myEntry = -1;
+        }
         Contact best{};
         float bestDist = 3.402823466e+38f;
-        int bestTri = -1;
-        int seen = 0;
-        for (int h = 0; h < HW && seen < MAX_CAR_TRI_PAIRS; h++)
+        bool have = false;
+        if (myEntry >= 0)
         {
-            for (unsigned m = x.hits[(long long)h * p.carStride + i]; m && seen < MAX_CAR_TRI_PAIRS; m &= m - 1)
+            const float4 q0 = __ldg(&arena.cellV[3 * myEntry]);
+            const float4 q1 = __ldg(&arena.cellV[3 * myEntry + 1]);
+            const float4 q2 = __ldg(&arena.cellV[3 * myEntry + 2]);
+            const LocalTri lt = localTriangle(cen, rot, V3{ q0.x, q0.y, q0.z }, V3{ q1.x, q1.y, q1.z },
+                                              V3{ q2.x, q2.y, q2.z });
+            const Sat sat = carTriSat(lt);
+            pairContacts(lt, sat, [&](const Contact& c) {
+                if (nearManifoldPoint(pts, planeCount, c.carPos)) return;
+                const float d = -c.depth;
+                if (d < bestDist)
+                {
+                    bestDist = d;
+                    best = c;
+                    have = true;
+                }
+            });
+        }
+        // Deepest over the hits, the earliest hit on ties.
+        float key = have ? bestDist : 3.402823466e+38f;
+        int owner = have ? lane : 32;
+        #pragma unroll
+        for (int off = 16; off > 0; off >>= 1)
+        {
+            const float ok = __shfl_xor_sync(FULL, key, off);
+            const int oo = __shfl_xor_sync(FULL, owner, off);
+            if (ok < key || (ok == key && oo < owner))
             {
-                seen++;
-                const int k = h * 32 + __ffs(m) - 1;
-                const int tri = __ldg(&arena.cellTris[cellFirst + k]);
-                V3 v0, v1, v2;
-                int flags;
-                loadTri(arena, tri, v0, v1, v2, flags);
-                const LocalTri lt = localTriangle(cen, rot, v0, v1, v2);
-                const Sat sat = carTriSat(lt);
-                pairContacts(lt, sat, [&](const Contact& c) {
-                    if (nearManifoldPoint(pts, planeCount, c.carPos)) return;
-                    const float d = -c.depth;
-                    if (d < bestDist)
-                    {
-                        bestDist = d;
-                        best = c;
-                        bestTri = tri;
-                    }
-                });
+                key = ok;
+                owner = oo;
             }
         }
-        if (bestTri >= 0)
+        if (owner < 32)
         {
-            V3 v0, v1, v2;
-            int flags;
-            loadTri(arena, bestTri, v0, v1, v2, flags);
-            adjustInternalEdge(localTriangle(cen, rot, v0, v1, v2), triAngles(arena, bestTri), best);
-            addManifoldPoint(pts, cnt, contactToManifold(best, cen, rot));
+            Contact c;
+            c.carPos = V3{ __shfl_sync(FULL, best.carPos.x, owner), __shfl_sync(FULL, best.carPos.y, owner),
+                           __shfl_sync(FULL, best.carPos.z, owner) };
+            c.arenaPos = V3{ __shfl_sync(FULL, best.arenaPos.x, owner), __shfl_sync(FULL, best.arenaPos.y, owner),
+                             __shfl_sync(FULL, best.arenaPos.z, owner) };
+            c.normal = V3{ __shfl_sync(FULL, best.normal.x, owner), __shfl_sync(FULL, best.normal.y, owner),
+                           __shfl_sync(FULL, best.normal.z, owner) };
+            c.depth = __shfl_sync(FULL, best.depth, owner);
+            const int e = __shfl_sync(FULL, myEntry, owner);
+            const float4 q0 = __ldg(&arena.cellV[3 * e]);
+            const float4 q1 = __ldg(&arena.cellV[3 * e + 1]);
+            const float4 q2 = __ldg(&arena.cellV[3 * e + 2]);
+            const int tri = __ldg(&arena.cellTris[e]);
+            adjustInternalEdge(localTriangle(cen, rot, V3{ q0.x, q0.y, q0.z }, V3{ q1.x, q1.y, q1.z },
+                                             V3{ q2.x, q2.y, q2.z }),
+                               triAngles(arena, tri), c);
+            addManifoldPoint(pts, cnt, contactToManifold(c, cen, rot));
         }
-        if (cnt > 0)
-        {
-            solveCarManifold(body, pts, cnt);
-            integrateSplitCorrection(body);
-        }
-        cars.n(C_MAN_COUNT, i) = cnt;
-        cars.setv(C_MAN_N0, i, cnt > 0 ? pts[0].worldNormal : v3zero());
-        body.vel = body.vel + body.extVel + body.deltaVel;
-        body.ang = body.ang + body.extAng + body.deltaAng;
-        storeCarBody(cars, i, body);
+        if (lane == 0) finishContactCar(cars, i, body, pts, cnt);
+        __syncwarp();
     }
 }
 
@@ -1531,7 +1610,7 @@ __global__ void __launch_bounds__(FIN_THREADS) finishKernel(TickParams p, StageS
     {
         // The per-tick work lists are consumed; empty them for the next tick.
         *x.ballCount = 0;
-        *x.heavyCount = 0;
+        for (int c = 0; c < HEAVY_CLASSES; c++) x.heavyCount[c] = 0;
     }
     if (tid < simsHere) ballFinishStage(cars, sims, s0 + tid, nCars, tick, x.ball, (int)p.simStride);
     __syncthreads();
@@ -1688,7 +1767,7 @@ int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch&
         y.keys = x.keys + c0;
         y.heavyBody = x.heavyBody + c0;
         y.heavyList = x.heavyList + c0;
-        y.heavyCount = x.heavyCount + g;
+        y.heavyCount = x.heavyCount + g * HEAVY_CLASSES;
         y.ball = x.ball + s0;
         y.ballList = x.ballList + s0;
         y.ballCount = x.ballCount + g;
@@ -1707,15 +1786,30 @@ int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch&
             const int n = q.nSim * q.nCars;
             const int simsPerFin = FIN_THREADS / q.nCars;
             const int ballBlocks = std::max(1, std::min((q.nSim + BALL_WARPS - 1) / BALL_WARPS, sms * 8 / nG));
-            const int contactBlocks = std::max(1, std::min((n + SOLVE_BLOCK - 1) / SOLVE_BLOCK, sms * 4 / nG));
+            const int contactBlocks = std::max(1, std::min((n + SOLVE_BLOCK - 1) / SOLVE_BLOCK, sms * 2 / nG));
+            const int meshBlocks = std::max(1, std::min((n + SOLVE_BLOCK - 1) / SOLVE_BLOCK, sms * 4 / nG));
+            const bool timed = g == 0 && t == p.nTicks - 1 && aux.stageEvents[0];
+            int k = 0;
+            auto mark = [&]() {
+                if (timed) cudaEventRecord((cudaEvent_t)aux.stageEvents[k++], sq);
+            };
+            mark();
             ballPrepKernel<<<(q.nSim + 255) / 256, 256, 0, sq>>>(q, y);
+            mark();
             flatKernel<<<(n + CAND_BLOCK - 1) / CAND_BLOCK, CAND_BLOCK, candSmem, sq>>>(q, a, y, t);
+            mark();
             rayCtlKernel<<<(n + RAY_BLOCK - 1) / RAY_BLOCK, RAY_BLOCK, 0, sq>>>(q, a, y, t);
+            mark();
             suspKernel<<<(n + SOLVE_BLOCK - 1) / SOLVE_BLOCK, SOLVE_BLOCK, 0, sq>>>(q, a, y, t);
-            contactKernel<<<contactBlocks, SOLVE_BLOCK, 0, sq>>>(q, a, y, t);
+            mark();
+            contactKernel<<<contactBlocks + meshBlocks, SOLVE_BLOCK, 0, sq>>>(q, a, y, t, contactBlocks);
+            mark();
             carCarKernel<<<(q.nSim + CC_BLOCK - 1) / CC_BLOCK, CC_BLOCK, 0, sq>>>(q, t);
+            mark();
             ballKernel<<<ballBlocks, BALL_WARPS * 32, 0, sq>>>(q, a, y, t);
+            mark();
             finishKernel<<<(q.nSim + simsPerFin - 1) / simsPerFin, FIN_THREADS, 0, sq>>>(q, y, t, simsPerFin);
+            mark();
         }
     for (int g = 0; g < nG; g++)
     {

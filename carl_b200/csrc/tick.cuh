@@ -51,8 +51,9 @@ struct StageScratch
     unsigned* wheelBits;    // [carStride] wheels with a ray contact this tick
     unsigned long long* keys;  // [4][carStride] wheel ray minimum (distance bits, candidate)
     float* heavyBody;       // [18][carStride] velocities after the suspension of listed cars
-    int* heavyList;         // [carStride] cars with possible plane / mesh contacts, this tick
-    int* heavyCount;        // [slices] entries of each slice's heavyList; zero between ticks
+    int* heavyList;         // [HEAVY_CLASSES][carStride] cars with possible plane contacts only / with
+                            // SAT hits, this tick
+    int* heavyCount;        // [slices][HEAVY_CLASSES] entries of each list; zero between ticks
     float* ball;            // [15][simStride] ball stage hand-over values
     int* ballList;          // [simStride] sims whose ball is moving (arena work), this tick
     int* ballCount;         // [slices] entries of each slice's ballList; zero between ticks
@@ -69,6 +70,13 @@ int tickThreads(int tileSims, int nCars);
 // Launches ceil(nSim / tileSims) CTAs on `stream`.
 int launchTick(const TickParams& p, const ArenaDev& a, void* stream);
 
+// Contact work lists: cars with plane contacts only, cars with SAT hits.
+constexpr int HEAVY_CLASSES = 2;
+
+// Stage kernels of one tick of the staged path, in launch order:
+// ballPrep, flat, rayCtl, susp, contact, carCar, ball, finish.
+constexpr int STAGE_KERNELS = 8;
+
 // Streams and events of the staged path (cudaStream_t / cudaEvent_t): the sims
 // are split into `groups` slices stepped concurrently on streams[0..groups).
 struct StageStreams
@@ -77,6 +85,8 @@ struct StageStreams
     void* streams[8];
     void* join[8];    // event per slice: its last kernel
     void* fork;       // event: work queued on the env stream before the launch
+    void* stageEvents[STAGE_KERNELS + 1];  // optional: timing events around slice 0's stage kernels
+                                           // in the last tick of the launch
 };
 
 // The same ticks as a sequence of stage kernels over the state in global memory.

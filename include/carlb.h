@@ -275,9 +275,18 @@ carlb_status carlb_write_field(carlb_env* env, carlb_field field, const void* ho
  * car-car contact counts.  Off by default. */
 carlb_status carlb_set_diagnostics(carlb_env* env, int32_t enabled);
 
-/* ---- per-stage kernel timing (device time of the last carlb_ticks call) ---- */
-/* Milliseconds spent in the fused tick kernel over the last carlb_ticks call. */
+/* ---- kernel timing (device time of the last carlb_ticks / carlb_env_step call) ---- */
+/* Milliseconds between the start of the first and the end of the last tick
+ * kernel of the last call (all stages and sim slices). */
 carlb_status carlb_last_tick_ms(const carlb_env* env, float* ms);
+/* Staged path only: when enabled, the last tick of every call records CUDA
+ * events around each stage kernel of the first sim slice (on that slice's
+ * stream).  No counterpart in the reference (profiling aid). */
+carlb_status carlb_set_stage_timing(carlb_env* env, int32_t enabled);
+/* Durations (ms) of the stage kernels of the last timed tick, in launch order:
+ * ball prelude, candidates (flat), ray finish + controls, suspension, contact
+ * solve, car-car, ball arena, finish.  Waits for that tick to complete. */
+carlb_status carlb_stage_times(carlb_env* env, float* ms, int32_t capacity, int32_t* count);
 
 #ifdef __cplusplus
 }
