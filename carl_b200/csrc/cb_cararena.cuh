@@ -460,16 +460,19 @@ CB_D void applyRow(Body& b, const Row& r, float impulse)
     b.deltaAng = b.deltaAng + r.angular * impulse;
 }
 
-// Solves one car against its manifold; returns nothing, updates the body's
-// delta / push velocities.
-CB_D void solveCarManifold(Body& b, const MPoint* p, int count)
+// Solves one car against its manifold of N points; updates the body's delta /
+// push velocities.  N is a compile-time constant so the rows stay in registers.
+template <int N>
+CB_D void solveCarManifoldN(Body& b, const MPoint* p)
 {
-    Row normalRow[MAX_CAR_MANIFOLD_POINTS], frictionRow[MAX_CAR_MANIFOLD_POINTS];
+    constexpr int count = N;
+    Row normalRow[N], frictionRow[N];
     const V3 centerOffset = b.cen - b.pos;
     const V3 totalVel = b.vel + b.extVel;
     const V3 totalAng = b.ang + b.extAng;
     constexpr float invDt = 1.f / PHYS_DT;
 
+    #pragma unroll
     for (int i = 0; i < count; i++)
     {
         const V3 relPos = centerOffset + rotate(b.rot, p[i].carPos);
@@ -514,6 +517,7 @@ CB_D void solveCarManifold(Body& b, const MPoint* p, int count)
     // Split impulses: position correction without changing reported velocity.
     for (int iter = 0; iter < CAR_SOLVER_ITERS; iter++)
     {
+        #pragma unroll
         for (int i = 0; i < count; i++)
         {
             Row& r = normalRow[i];
@@ -527,12 +531,14 @@ CB_D void solveCarManifold(Body& b, const MPoint* p, int count)
 
     for (int iter = 0; iter < CAR_SOLVER_ITERS; iter++)
     {
+        #pragma unroll
         for (int i = 0; i < count; i++)
         {
             Row& r = normalRow[i];
             const float rv = rowVel(r, b.deltaVel, b.deltaAng);
             applyRow(b, r, solveLowerImpulse(r.rhs, 0.f, r.jacInv, rv, r.lower, r.applied));
         }
+        #pragma unroll
         for (int i = 0; i < count; i++)
         {
             const float maxImpulse = CAR_WORLD_FRICTION * normalRow[i].applied;
@@ -543,6 +549,18 @@ CB_D void solveCarManifold(Body& b, const MPoint* p, int count)
             const float rv = rowVel(f, b.deltaVel, b.deltaAng);
             applyRow(b, f, solveImpulse(f.rhs, 0.f, f.jacInv, rv, f.lower, f.upper, f.applied));
         }
+    }
+}
+
+CB_D void solveCarManifold(Body& b, const MPoint* p, int count)
+{
+    switch (count)
+    {
+    case 1: solveCarManifoldN<1>(b, p); break;
+    case 2: solveCarManifoldN<2>(b, p); break;
+    case 3: solveCarManifoldN<3>(b, p); break;
+    case 4: solveCarManifoldN<4>(b, p); break;
+    default: break;
     }
 }
 

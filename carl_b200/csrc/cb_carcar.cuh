@@ -239,9 +239,14 @@ CB_D void pairApply(Body& a, Body& b, const PairRow& r, float impulse, bool spli
     ab = ab - r.angularB * impulse;
 }
 
-CB_D void solvePair(Body& a, Body& b, const CCContact* c, int count)
+// Two-body solve of N contacts; N is a compile-time constant so the rows stay
+// in registers.
+template <int N>
+CB_D void solvePairN(Body& a, Body& b, const CCContact* c)
 {
-    PairRow nr[MAX_CAR_MANIFOLD_POINTS], fr[MAX_CAR_MANIFOLD_POINTS];
+    constexpr int count = N;
+    PairRow nr[N], fr[N];
+    #pragma unroll
     for (int i = 0; i < count; i++)
     {
         const V3 relA = a.cen - a.pos + rotate(a.rot, c[i].carPosA);
@@ -268,6 +273,7 @@ CB_D void solvePair(Body& a, Body& b, const CCContact* c, int count)
         fr[i] = f;
     }
     for (int iter = 0; iter < CAR_SOLVER_ITERS; iter++)
+        #pragma unroll
         for (int i = 0; i < count; i++)
         {
             PairRow& r = nr[i];
@@ -276,12 +282,14 @@ CB_D void solvePair(Body& a, Body& b, const CCContact* c, int count)
         }
     for (int iter = 0; iter < CAR_SOLVER_ITERS; iter++)
     {
+        #pragma unroll
         for (int i = 0; i < count; i++)
         {
             PairRow& r = nr[i];
             const float rv = pairVel(r, a.deltaVel, a.deltaAng, b.deltaVel, b.deltaAng);
             pairApply(a, b, r, solveLowerImpulse(r.rhs, 0.f, r.jacInv, rv, 0.f, r.applied), false);
         }
+        #pragma unroll
         for (int i = 0; i < count; i++)
         {
             const float maxImpulse = CARCAR_COLLISION_FRICTION * nr[i].applied;
@@ -290,6 +298,18 @@ CB_D void solvePair(Body& a, Body& b, const CCContact* c, int count)
             const float rv = pairVel(f, a.deltaVel, a.deltaAng, b.deltaVel, b.deltaAng);
             pairApply(a, b, f, solveImpulse(f.rhs, 0.f, f.jacInv, rv, -maxImpulse, maxImpulse, f.applied), false);
         }
+    }
+}
+
+CB_D void solvePair(Body& a, Body& b, const CCContact* c, int count)
+{
+    switch (count)
+    {
+    case 1: solvePairN<1>(a, b, c); break;
+    case 2: solvePairN<2>(a, b, c); break;
+    case 3: solvePairN<3>(a, b, c); break;
+    case 4: solvePairN<4>(a, b, c); break;
+    default: break;
     }
 }
 
