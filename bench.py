@@ -159,16 +159,17 @@ def control_pool(n_cars_total: int, count: int, seed: int):
     return [workloads.controls(rng, n_cars_total) for _ in range(count)]
 
 
-def traffic_per_launch(stage: str) -> float | None:
-    """DRAM bytes per launch of a stage kernel at this workload, from the
-    committed ncu summary of the staged tick (None when not captured)."""
+def traffic_per_launch(stage: str, n_sim: int) -> float | None:
+    """DRAM bytes per launch of a stage kernel, from the committed ncu summary
+    of the staged tick (stated for n_sim = 32768, 2 slices; traffic grows with
+    the sims, so it is scaled to this run's n_sim).  None when not captured."""
     path = ROOT / "profiles" / "staged_tick_3v3_32768.md"
     if not path.exists():
         return None
     key = f"traffic_bytes_per_launch[{stage}]:"
     for line in path.read_text().splitlines():
         if line.startswith(key):
-            return float(line.split(":", 1)[1].split()[0])
+            return float(line.split(":", 1)[1].split()[0]) * n_sim / 32768
     return None
 
 
@@ -324,7 +325,11 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     kernel_ms = []
     stage_ms: dict[str, list[float]] = {}
-    env.set_stage_timing(True)
+    try:
+        env.set_stage_timing(True)
+        staged = True
+    except capi.CarlbError:  # the fused path (CARLB_TICK_PATH=fused) has one kernel per launch
+        staged = False
     sampler = ClockSampler(device)
     sampler.start()
     barrier()
@@ -338,8 +343,9 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         ends[i].record(stream)
         env.synchronize()
         kernel_ms.append(env.last_tick_ms())
-        for name, ms in env.stage_times().items():
-            stage_ms.setdefault(name, []).append(ms)
+        if staged:
+            for name, ms in env.stage_times().items():
+                stage_ms.setdefault(name, []).append(ms)
     torch.cuda.synchronize()
     barrier()
     wall = time.perf_counter() - wall0
@@ -351,7 +357,8 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     step_ms, kern_ms = float(t[0]), float(t[1])
-    env.set_stage_timing(False)
+    if staged:
+        env.set_stage_timing(False)
     stage_avg = {k: sum(v) / len(v) for k, v in stage_ms.items()}
 
     agent_ticks_rank = n_total_cars * TICKS_PER_STEP * args.steps
@@ -390,23 +397,29 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
 
     # ---- roofline of the dominant stage kernel, and of the whole tick ----
     peak, peak_kind = measured_hbm_peak()
-    modelled = {k: v for k, v in stage_avg.items() if k in STAGE_BYTES}
-    dom = max(modelled, key=modelled.get)
-    per_car, per_sim = STAGE_BYTES[dom]
-    dom_bytes = per_car * n_total_cars + per_sim * args.n_sim
-    dom_ms = stage_avg[dom]
-    achieved = dom_bytes / (dom_ms / 1e3) / 1e9
-    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "traffic": traffic_per_launch(dom), "peak_kind": peak_kind, "kernel": dom + "Kernel",
-                "launch_ms": dom_ms, "algorithmic_bytes_per_launch": dom_bytes,
-                "stage_ms": {k: round(v, 4) for k, v in stage_avg.items()},
-                "largest_stage": max(stage_avg, key=stage_avg.get)}
     bpat = bytes_per_agent_tick(n_cars)
     tick_ms = kern_ms / args.steps / TICKS_PER_STEP
     tick_achieved = bpat * n_total_cars / (tick_ms / 1e3) / 1e9
     roofline_tick = {"bound": "hbm", "achieved": tick_achieved, "peak": peak, "unit": "GB/s",
                      "frac": tick_achieved / peak, "model": "CARLB-v1", "bytes_per_agent_tick": bpat,
                      "tick_ms": tick_ms}
+    if staged:
+        # A stage kernel launch covers one sim slice (the timed one is slice 0).
+        groups = world_groups(args)
+        modelled = {k: v for k, v in stage_avg.items() if k in STAGE_BYTES}
+        dom = max(modelled, key=modelled.get)
+        per_car, per_sim = STAGE_BYTES[dom]
+        dom_bytes = (per_car * n_total_cars + per_sim * args.n_sim) / groups
+        dom_ms = stage_avg[dom]
+        achieved = dom_bytes / (dom_ms / 1e3) / 1e9
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                    "traffic": traffic_per_launch(dom, args.n_sim), "peak_kind": peak_kind, "kernel": dom + "Kernel",
+                    "launch_ms": dom_ms, "algorithmic_bytes_per_launch": dom_bytes, "sim_slices": groups,
+                    "stage_ms": {k: round(v, 4) for k, v in stage_avg.items()},
+                    "largest_stage": max(stage_avg, key=stage_avg.get)}
+    else:
+        roofline = dict(roofline_tick, kernel="tickKernel (fused, 8 ticks per launch)", peak_kind=peak_kind,
+                        traffic=None, launch_ms=kern_ms / args.steps)
 
     cpu = None
     if snap0 is not None:
@@ -432,7 +445,8 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
                    "ticks_per_step": TICKS_PER_STEP, "sims_total": args.n_sim * world,
                    "parallelism": f"sim-sharded x{world}", "l2": "256 MiB buffer written between timed steps",
                    "wall_s": wall},
-        "clocks": clocks, "e2e": e2e, "gpu_launches": args.steps * launches_per_step(world_groups(args)),
+        "clocks": clocks, "e2e": e2e,
+        "gpu_launches": args.steps * (launches_per_step(world_groups(args)) if staged else 1),
         "roofline": roofline, "roofline_tick": roofline_tick, "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)
