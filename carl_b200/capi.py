@@ -97,6 +97,7 @@ def load() -> ctypes.CDLL:
     lib.carlb_env_step.argtypes = [vp, i32, vp]
     lib.carlb_ticks.argtypes = [vp, i32, vp, i32]
     lib.carlb_ticks_host.argtypes = [vp, i32, vp, i32, vp]
+    lib.carlb_ticks_static_scratch.argtypes = [vp, i32, vp, i32]
     lib.carlb_reset.argtypes = [vp]
     lib.carlb_reset_dones.argtypes = [vp]
     lib.carlb_apply_reset_state.argtypes = [vp, i32] + [vp] * 8 + [i32] + [vp] * 7
@@ -207,6 +208,12 @@ class Env:
     def ticks(self, kind: int, actions, n_ticks: int) -> None:
         keep = self._order_after_torch(actions)
         self._check(self._lib.carlb_ticks(self._h, kind, _ptr(actions), n_ticks))
+        self._keep_until_read(keep)
+
+    def ticks_static_scratch(self, kind: int, actions, n_ticks: int) -> None:
+        """carlb_ticks with the fixed-size static stage scratch (allocates nothing)."""
+        keep = self._order_after_torch(actions)
+        self._check(self._lib.carlb_ticks_static_scratch(self._h, kind, _ptr(actions), n_ticks))
         self._keep_until_read(keep)
 
     def ticks_host(self, kind: int, host_actions: np.ndarray, n_ticks: int, host_rewards: np.ndarray | None = None) -> None:

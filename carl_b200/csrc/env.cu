@@ -559,6 +559,85 @@ carlb_status carlb_ticks(carlb_env* e, carlb_action_kind kind, const void* actio
     return launchTicks(e, kind, n);
 }
 
+carlb_status carlb_ticks_static_scratch(carlb_env* e, carlb_action_kind kind, const void* actions, int32_t n)
+{
+    if (!e) return fail(nullptr, CARLB_ERR_VALUE, "env is null");
+    if (n < 0) return fail(e, CARLB_ERR_VALUE, "n_ticks must be non-negative");
+    if (!e->staged) return fail(e, CARLB_ERR_STATE, "the static-scratch ticks need the staged tick path");
+    ECHECK(e, cudaSetDevice(e->cfg.device));
+    void* base = nullptr;
+    size_t capacity = 0;
+    const int aerr = staticScratchAddress(&base, &capacity);
+    if (aerr) return cudaFail(e, (cudaError_t)aerr, "static scratch lookup");
+
+    // Carve the stage scratch out of the fixed array (each part 256-byte aligned).
+    const size_t cs = (size_t)e->carStride, ss = (size_t)e->simStride;
+    size_t off = 0;
+    auto take = [&](size_t bytes) -> size_t {
+        const size_t at = (off + 255) & ~(size_t)255;
+        off = at + bytes;
+        return at;
+    };
+    const size_t oFirst = take(cs * 4), oCnt = take(cs * 4), oRay = take(16 * cs * 4);
+    const size_t oHits = take((size_t)e->hitWords * cs * 4), oWheel = take(cs * 4), oKeys = take(4 * cs * 8);
+    const size_t oHeavyBody = take(18 * cs * 4), oHeavyList = take((size_t)HEAVY_CLASSES * cs * 4);
+    const size_t oHeavyCount = take(8 * HEAVY_CLASSES * 4), oBall = take(15 * ss * 4), oBallList = take(ss * 4);
+    const size_t oBallCount = take(8 * 4);
+    if (off > capacity)
+        return fail(e, CARLB_ERR_VALUE,
+                    "env needs " + std::to_string(off) + " bytes of stage scratch; the static scratch holds " +
+                        std::to_string(capacity));
+    char* b = static_cast<char*>(base);
+    StageScratch x{};
+    x.first = reinterpret_cast<int*>(b + oFirst);
+    x.cnt = reinterpret_cast<int*>(b + oCnt);
+    x.ray = reinterpret_cast<float*>(b + oRay);
+    x.hits = reinterpret_cast<unsigned*>(b + oHits);
+    x.wheelBits = reinterpret_cast<unsigned*>(b + oWheel);
+    x.keys = reinterpret_cast<unsigned long long*>(b + oKeys);
+    x.heavyBody = reinterpret_cast<float*>(b + oHeavyBody);
+    x.heavyList = reinterpret_cast<int*>(b + oHeavyList);
+    x.heavyCount = reinterpret_cast<int*>(b + oHeavyCount);
+    x.ball = reinterpret_cast<float*>(b + oBall);
+    x.ballList = reinterpret_cast<int*>(b + oBallList);
+    x.ballCount = reinterpret_cast<int*>(b + oBallCount);
+
+    carlb_status s = stageActions(e, kind, actions, cudaMemcpyDeviceToDevice);
+    if (s != CARLB_OK) return s;
+    // The work-list counters start at zero (every other scratch word is written
+    // before it is read within a tick).
+    ECHECK(e, cudaMemsetAsync(x.heavyCount, 0, 8 * HEAVY_CLASSES * 4, e->stream));
+    ECHECK(e, cudaMemsetAsync(x.ballCount, 0, 8 * 4, e->stream));
+
+    TickParams p{};
+    p.car = e->car;
+    p.sim = e->sim;
+    p.carOut = e->carOut;
+    p.diagCar = e->diagnostics ? e->diagCar : nullptr;
+    p.diagSim = e->diagnostics ? e->diagSim : nullptr;
+    p.actions = e->actions;
+    p.carStride = e->carStride;
+    p.simStride = e->simStride;
+    p.globalCarBase = e->cfg.sim_offset * e->nCars;
+    p.actionKind = (int)kind;
+    p.nSim = e->cfg.n_sim;
+    p.nCars = e->nCars;
+    p.nBlue = e->cfg.n_blue;
+    p.seed = e->cfg.seed;
+    p.tick0 = e->tick;
+    p.nTicks = n;
+    p.tileSims = e->tileSims;
+    p.compatFlags = e->cfg.compat_flags;
+    StageStreams streams = e->stageStreams();
+    for (int k = 0; k <= STAGE_KERNELS; k++) streams.stageEvents[k] = nullptr;
+    ECHECK(e, cudaEventRecord(e->ev0, e->stream));
+    const int err = launchTickStaged(p, e->arena(), x, e->stream, streams);
+    if (err) return cudaFail(e, (cudaError_t)err, "tick kernel launch");
+    ECHECK(e, cudaEventRecord(e->ev1, e->stream));
+    e->tick += n;
+    return CARLB_OK;
+}
+
 carlb_status carlb_ticks_host(carlb_env* e, carlb_action_kind kind, const void* hostActions, int32_t n,
                               float* hostRewards)
 {

@@ -26,6 +26,7 @@
 #include "tick.cuh"
 
 #include <algorithm>
+#include <mutex>
 
 #include <cuda_runtime.h>
 
@@ -1697,6 +1698,33 @@ int launchTick(const TickParams& p, const ArenaDev& a, void* stream)
     return (int)cudaGetLastError();
 }
 
+
+// ---- fixed-size scratch for carlb_ticks_static_scratch --------------------------------------
+// A file-scope device array, so that entry point allocates nothing at call time.
+// Calls that overlap in time (any env, any stream) share it and race.
+static __device__ __align__(256) unsigned char g_staticScratch[STATIC_SCRATCH_BYTES];
+
+int staticScratchAddress(void** ptr, size_t* bytes)
+{
+    static std::mutex lock;
+    static void* cached[64] = {};
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return (int)err;
+    if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> guard(lock);
+    if (!cached[dev])
+    {
+        void* p = nullptr;
+        err = cudaGetSymbolAddress(&p, g_staticScratch);
+        if (err != cudaSuccess) return (int)err;
+        if (!p) return (int)cudaErrorInvalidSymbol;
+        cached[dev] = p;
+    }
+    *ptr = cached[dev];
+    *bytes = STATIC_SCRATCH_BYTES;
+    return 0;
+}
 
 size_t stageCandSmemBytes(int hitWords)
 {

@@ -89,6 +89,11 @@ struct StageStreams
                                            // in the last tick of the launch
 };
 
+// Capacity of the file-scope device scratch used by carlb_ticks_static_scratch.
+constexpr size_t STATIC_SCRATCH_BYTES = 64ull << 20;
+// Device address of that scratch on the current device (looked up once per device).
+int staticScratchAddress(void** ptr, size_t* bytes);
+
 // The same ticks as a sequence of stage kernels over the state in global memory.
 int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch& x, void* stream,
                      const StageStreams& aux);

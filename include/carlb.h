@@ -225,6 +225,16 @@ carlb_status carlb_ticks(carlb_env* env, carlb_action_kind kind, const void* act
  * may be NULL) happen on the env stream; returns after the stream drains. */
 carlb_status carlb_ticks_host(carlb_env* env, carlb_action_kind kind, const void* host_actions,
                               int32_t n_ticks, float* host_rewards);
+/* Same ticks as carlb_ticks, with the stage scratch taken from a fixed-size
+ * file-scope device array (64 MiB) instead of the env's own scratch, so the call
+ * allocates nothing (no cudaMalloc/cudaFree, no allocating library call).  The
+ * array's address is looked up once per device.  Returns CARLB_ERR_VALUE when the
+ * env needs more scratch than the array holds, CARLB_ERR_STATE on the fused path.
+ * The array is shared: calls that overlap in time (any env, any stream) race, so
+ * serialise them.  The first call on a device does the one-time lookup, so make
+ * it before capturing any stream.  No counterpart in the reference. */
+carlb_status carlb_ticks_static_scratch(carlb_env* env, carlb_action_kind kind, const void* actions,
+                                        int32_t n_ticks);
 carlb_status carlb_reset(carlb_env* env);
 /* Auto-reset of finished sims (src/State/Reset.cuh:82-171 semantics). */
 carlb_status carlb_reset_dones(carlb_env* env);
