@@ -16,6 +16,10 @@ namespace cb {
 
 // ---- sphere vs triangle ---------------------------------------------------------------
 
+// Whether a car touched the ball on the tick before `tick` (arena contacts are
+// solved before car-ball contacts, so that is the hit that matters).
+CB_HD bool ballHitPreviousTick(int hitTick, int tick) { return hitTick >= 0 && tick > 0 && hitTick == tick - 1; }
+
 struct BallContact
 {
     V3 point, relPos, normal;

@@ -290,7 +290,7 @@ __device__ V3 ballArenaSolve(const SmemSoa& cars, const SmemSoa& sims, int s, in
         for (int k = 0; k < nCars; k++)
         {
             const int hitTick = cars.n(C_BALL_HIT_TICK, carBase + k);
-            wasHit |= hitTick >= 0 && tick > 0 && hitTick == tick - 1;
+            wasHit |= ballHitPreviousTick(hitTick, tick);
         }
         BallBody body;
         body.pos = center;

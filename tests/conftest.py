@@ -51,7 +51,7 @@ def pytest_collection_modifyitems(config, items):
 def oracle_built() -> Path:
     """oracle/_ref/ built from the reference sources (here) or prebuilt (GPU box)."""
     ref = ROOT / "oracle" / "_ref"
-    need = [ref / "libcarlref_cpu.so", ref / "arena.obj"]
+    need = [ref / "libcarlref_cpu.so", ref / "libcarlref_ka.so", ref / "arena.obj"]
     if not all(p.exists() for p in need):
         if not REFERENCE.exists():
             pytest.skip("oracle not built and the reference tree is absent")

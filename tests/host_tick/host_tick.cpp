@@ -8,14 +8,7 @@
 // The stage split mirrors carl_b200/csrc/tick.cu: candidate rays and SAT in
 // candidate order, the first 32 SAT hits, per-sim car-car pairs then ball with
 // ball-arena triangles in ascending order.  TEST INFRASTRUCTURE.
-#include <cmath>
-
-inline float rsqrtf(float x) { return 1.f / sqrtf(x); }
-inline void fast_sincos(float x, float* s, float* c)
-{
-    *s = sinf(x);
-    *c = cosf(x);
-}
+#include "host_intrinsics.h"
 
 #include <cstring>
 #include <string>
@@ -331,7 +324,7 @@ void HostEnv::step(const Controls* ctl)
             for (int k = 0; k < nCars; k++)
             {
                 const int ht = C.n(C_BALL_HIT_TICK, sb + k);
-                wasHit |= ht >= 0 && tick > 0 && ht == tick - 1;
+                wasHit |= ballHitPreviousTick(ht, tick);
             }
             BallBody body;
             body.pos = center;

@@ -13,8 +13,9 @@ from carl_b200 import capi
 
 ROOT = Path(__file__).resolve().parents[1]
 SRC = ROOT / "tests" / "host_tick" / "host_tick.cpp"
+KA = ROOT / "tests" / "host_tick" / "known_answers.cpp"
 LIB = ROOT / "tests" / "host_tick" / "_build" / "libhosttick.so"
-DEPS = [SRC, *sorted((ROOT / "carl_b200" / "csrc").glob("*.cuh")), *sorted((ROOT / "carl_b200" / "csrc").glob("*.hpp")),
+DEPS = [SRC, KA, ROOT / "tests" / "host_tick" / "host_intrinsics.h", *sorted((ROOT / "carl_b200" / "csrc").glob("*.cuh")), *sorted((ROOT / "carl_b200" / "csrc").glob("*.hpp")),
         ROOT / "carl_b200" / "csrc" / "arena.cpp", ROOT / "carl_b200" / "csrc" / "tables.cpp"]
 _lib = None
 
@@ -23,9 +24,14 @@ def build() -> Path:
     if not LIB.exists() or any(d.stat().st_mtime > LIB.stat().st_mtime for d in DEPS):
         LIB.parent.mkdir(exist_ok=True)
         subprocess.run(["g++", "-std=c++17", "-O2", "-ffp-contract=off", "-fPIC", "-shared", "-include", "algorithm",
-                        "-o", str(LIB), str(SRC), str(ROOT / "carl_b200/csrc/arena.cpp"),
+                        "-o", str(LIB), str(SRC), str(KA), str(ROOT / "carl_b200/csrc/arena.cpp"),
                         str(ROOT / "carl_b200/csrc/tables.cpp")], check=True)
     return LIB
+
+
+def lib():
+    """The host build library (for the known-answer functions)."""
+    return _load()
 
 
 def _load():
