@@ -95,7 +95,10 @@ struct carlb_env
     cudaEvent_t evFork = nullptr;
     bool stageTiming = false;
     bool stageTimed = false;  // the last launch recorded stage events
-    cudaEvent_t stageEv[STAGE_KERNELS + 1] = {};
+    cudaEvent_t stageEv[2 * STAGE_KERNELS] = {};
+    bool ballSide = true;  // ball arena stage on a side stream per slice (CARLB_BALL_STREAM=0 disables)
+    cudaStream_t ballStream[8] = {};
+    cudaEvent_t tickStart[8] = {}, ballDone[8] = {};
 
     float *obs = nullptr, *tobs = nullptr, *packed = nullptr, *tpacked = nullptr, *rewards = nullptr;
     uint8_t *dones = nullptr, *overtime = nullptr, *tovertime = nullptr;
@@ -139,7 +142,13 @@ struct carlb_env
             s.join[g] = groupJoin[g];
         }
         s.fork = evFork;
-        for (int k = 0; k <= STAGE_KERNELS; k++) s.stageEvents[k] = stageTiming ? stageEv[k] : nullptr;
+        for (int k = 0; k < 2 * STAGE_KERNELS; k++) s.stageEvents[k] = stageTiming ? stageEv[k] : nullptr;
+        for (int g = 0; g < 8; g++)
+        {
+            s.ballStreams[g] = ballSide ? ballStream[g] : nullptr;
+            s.tickStart[g] = tickStart[g];
+            s.ballDone[g] = ballDone[g];
+        }
         return s;
     }
     ArenaDev arena() const { return ArenaDev{ triV, triAng, cellStart, cellTris, hitWords, cellSph, carReach, cellV }; }
@@ -392,10 +401,17 @@ static carlb_status initEnv(carlb_env* p, const carlb_config* cfg)
         if (const char* g = std::getenv("CARLB_GROUPS")) p->groups = std::max(1, std::min(8, std::atoi(g)));
         // Slices of fewer than ~4k sims would leave the wide stages too small.
         p->groups = std::max(1, std::min(p->groups, cfg->n_sim / 4096));
+        if (const char* b = std::getenv("CARLB_BALL_STREAM")) p->ballSide = std::atoi(b) != 0;
         for (int g = 0; g < p->groups; g++)
         {
             ECHECK(p, cudaStreamCreateWithFlags(&p->groupStream[g], cudaStreamNonBlocking));
             ECHECK(p, cudaEventCreateWithFlags(&p->groupJoin[g], cudaEventDisableTiming));
+            if (p->ballSide)
+            {
+                ECHECK(p, cudaStreamCreateWithFlags(&p->ballStream[g], cudaStreamNonBlocking));
+                ECHECK(p, cudaEventCreateWithFlags(&p->tickStart[g], cudaEventDisableTiming));
+                ECHECK(p, cudaEventCreateWithFlags(&p->ballDone[g], cudaEventDisableTiming));
+            }
         }
         ECHECK(p, cudaEventCreateWithFlags(&p->evFork, cudaEventDisableTiming));
         ECHECK(p, allocZero(p, &p->scratch.first, (size_t)p->carStride));
@@ -531,7 +547,10 @@ carlb_status carlb_destroy(carlb_env* e)
     cudaSetDevice(e->cfg.device);
     if (e->stream) cudaStreamSynchronize(e->stream);
     for (int g = 0; g < 8; g++)
+    {
         if (e->groupStream[g]) cudaStreamSynchronize(e->groupStream[g]);
+        if (e->ballStream[g]) cudaStreamSynchronize(e->ballStream[g]);
+    }
     for (void* v : e->allocations) cudaFree(v);
     if (e->ev0) cudaEventDestroy(e->ev0);
     if (e->ev1) cudaEventDestroy(e->ev1);
@@ -539,9 +558,12 @@ carlb_status carlb_destroy(carlb_env* e)
     {
         if (e->groupJoin[g]) cudaEventDestroy(e->groupJoin[g]);
         if (e->groupStream[g]) cudaStreamDestroy(e->groupStream[g]);
+        if (e->tickStart[g]) cudaEventDestroy(e->tickStart[g]);
+        if (e->ballDone[g]) cudaEventDestroy(e->ballDone[g]);
+        if (e->ballStream[g]) cudaStreamDestroy(e->ballStream[g]);
     }
     if (e->evFork) cudaEventDestroy(e->evFork);
-    for (int k = 0; k <= STAGE_KERNELS; k++)
+    for (int k = 0; k < 2 * STAGE_KERNELS; k++)
         if (e->stageEv[k]) cudaEventDestroy(e->stageEv[k]);
     if (e->stream) cudaStreamDestroy(e->stream);
     delete e;
@@ -629,7 +651,7 @@ carlb_status carlb_ticks_static_scratch(carlb_env* e, carlb_action_kind kind, co
     p.tileSims = e->tileSims;
     p.compatFlags = e->cfg.compat_flags;
     StageStreams streams = e->stageStreams();
-    for (int k = 0; k <= STAGE_KERNELS; k++) streams.stageEvents[k] = nullptr;
+    for (int k = 0; k < 2 * STAGE_KERNELS; k++) streams.stageEvents[k] = nullptr;
     ECHECK(e, cudaEventRecord(e->ev0, e->stream));
     const int err = launchTickStaged(p, e->arena(), x, e->stream, streams);
     if (err) return cudaFail(e, (cudaError_t)err, "tick kernel launch");
@@ -918,7 +940,7 @@ carlb_status carlb_set_stage_timing(carlb_env* e, int32_t enabled)
     if (!e) return fail(nullptr, CARLB_ERR_VALUE, "env is null");
     if (!e->staged) return fail(e, CARLB_ERR_STATE, "stage timing needs the staged tick path");
     ECHECK(e, cudaSetDevice(e->cfg.device));
-    for (int k = 0; k <= STAGE_KERNELS && enabled; k++)
+    for (int k = 0; k < 2 * STAGE_KERNELS && enabled; k++)
         if (!e->stageEv[k]) ECHECK(e, cudaEventCreate(&e->stageEv[k]));
     e->stageTiming = enabled != 0;
     e->stageTimed = false;
@@ -930,10 +952,10 @@ carlb_status carlb_stage_times(carlb_env* e, float* ms, int32_t capacity, int32_
     if (!e || !count) return fail(e, CARLB_ERR_VALUE, "env or count is null");
     *count = 0;
     if (!e->stageTimed) return fail(e, CARLB_ERR_STATE, "no timed launch since stage timing was enabled");
-    ECHECK(e, cudaEventSynchronize(e->stageEv[STAGE_KERNELS]));
     for (int k = 0; k < STAGE_KERNELS && k < capacity; k++)
     {
-        ECHECK(e, cudaEventElapsedTime(&ms[k], e->stageEv[k], e->stageEv[k + 1]));
+        ECHECK(e, cudaEventSynchronize(e->stageEv[2 * k + 1]));
+        ECHECK(e, cudaEventElapsedTime(&ms[k], e->stageEv[2 * k], e->stageEv[2 * k + 1]));
         *count = k + 1;
     }
     return CARLB_OK;

@@ -1817,27 +1817,47 @@ int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch&
             const int contactBlocks = std::max(1, std::min((n + SOLVE_BLOCK - 1) / SOLVE_BLOCK, sms * 2 / nG));
             const int meshBlocks = std::max(1, std::min((n + SOLVE_BLOCK - 1) / SOLVE_BLOCK, sms * 4 / nG));
             const bool timed = g == 0 && t == p.nTicks - 1 && aux.stageEvents[0];
-            int k = 0;
-            auto mark = [&]() {
-                if (timed) cudaEventRecord((cudaEvent_t)aux.stageEvents[k++], sq);
+            // Events around stage k: stageEvents[2k] (start), [2k + 1] (end), on the
+            // stream the stage kernel runs on.
+            auto mark = [&](int k, bool end, cudaStream_t on) {
+                if (timed) cudaEventRecord((cudaEvent_t)aux.stageEvents[2 * k + (end ? 1 : 0)], on);
             };
-            mark();
-            ballPrepKernel<<<(q.nSim + 255) / 256, 256, 0, sq>>>(q, y);
-            mark();
+            // The ball's arena stage reads only the ball and the cars' last-hit ticks,
+            // which no car stage of this tick writes before the finish kernel, so with
+            // a side stream it runs beside the car stages.
+            cudaStream_t sb = aux.ballStreams[g] ? (cudaStream_t)aux.ballStreams[g] : sq;
+            if (sb != sq)
+            {
+                if ((err = cudaEventRecord((cudaEvent_t)aux.tickStart[g], sq)) != cudaSuccess) return (int)err;
+                if ((err = cudaStreamWaitEvent(sb, (cudaEvent_t)aux.tickStart[g], 0)) != cudaSuccess) return (int)err;
+            }
+            mark(0, false, sb);
+            ballPrepKernel<<<(q.nSim + 255) / 256, 256, 0, sb>>>(q, y);
+            mark(0, true, sb);
+            mark(6, false, sb);
+            ballKernel<<<ballBlocks, BALL_WARPS * 32, 0, sb>>>(q, a, y, t);
+            mark(6, true, sb);
+            if (sb != sq && (err = cudaEventRecord((cudaEvent_t)aux.ballDone[g], sb)) != cudaSuccess) return (int)err;
+            mark(1, false, sq);
             flatKernel<<<(n + CAND_BLOCK - 1) / CAND_BLOCK, CAND_BLOCK, candSmem, sq>>>(q, a, y, t);
-            mark();
+            mark(1, true, sq);
+            mark(2, false, sq);
             rayCtlKernel<<<(n + RAY_BLOCK - 1) / RAY_BLOCK, RAY_BLOCK, 0, sq>>>(q, a, y, t);
-            mark();
+            mark(2, true, sq);
+            mark(3, false, sq);
             suspKernel<<<(n + SOLVE_BLOCK - 1) / SOLVE_BLOCK, SOLVE_BLOCK, 0, sq>>>(q, a, y, t);
-            mark();
+            mark(3, true, sq);
+            mark(4, false, sq);
             contactKernel<<<contactBlocks + meshBlocks, SOLVE_BLOCK, 0, sq>>>(q, a, y, t, contactBlocks);
-            mark();
+            mark(4, true, sq);
+            mark(5, false, sq);
             carCarKernel<<<(q.nSim + CC_BLOCK - 1) / CC_BLOCK, CC_BLOCK, 0, sq>>>(q, t);
-            mark();
-            ballKernel<<<ballBlocks, BALL_WARPS * 32, 0, sq>>>(q, a, y, t);
-            mark();
+            mark(5, true, sq);
+            if (sb != sq && (err = cudaStreamWaitEvent(sq, (cudaEvent_t)aux.ballDone[g], 0)) != cudaSuccess)
+                return (int)err;
+            mark(7, false, sq);
             finishKernel<<<(q.nSim + simsPerFin - 1) / simsPerFin, FIN_THREADS, 0, sq>>>(q, y, t, simsPerFin);
-            mark();
+            mark(7, true, sq);
         }
     for (int g = 0; g < nG; g++)
     {

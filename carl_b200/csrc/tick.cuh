@@ -83,10 +83,13 @@ struct StageStreams
 {
     int groups;
     void* streams[8];
-    void* join[8];    // event per slice: its last kernel
-    void* fork;       // event: work queued on the env stream before the launch
-    void* stageEvents[STAGE_KERNELS + 1];  // optional: timing events around slice 0's stage kernels
-                                           // in the last tick of the launch
+    void* join[8];        // event per slice: its last kernel
+    void* fork;           // event: work queued on the env stream before the launch
+    void* ballStreams[8]; // optional side stream per slice for the ball's arena stage
+    void* tickStart[8];   // event per slice: the previous tick's finish (side stream waits)
+    void* ballDone[8];    // event per slice: the ball's arena stage (finish waits)
+    void* stageEvents[2 * STAGE_KERNELS];  // optional: start / end events of slice 0's stage
+                                           // kernels in the last tick of the launch
 };
 
 // Capacity of the file-scope device scratch used by carlb_ticks_static_scratch.
