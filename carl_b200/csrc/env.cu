@@ -99,6 +99,8 @@ struct carlb_env
     bool ballSide = true;  // ball arena stage on a side stream per slice (CARLB_BALL_STREAM=0 disables)
     cudaStream_t ballStream[8] = {};
     cudaEvent_t tickStart[8] = {}, ballDone[8] = {};
+    bool phaseOffset = true;  // slices alternate their wide stages (CARLB_PHASE_OFFSET=0 disables)
+    cudaEvent_t wideDone[8] = {};
 
     float *obs = nullptr, *tobs = nullptr, *packed = nullptr, *tpacked = nullptr, *rewards = nullptr;
     uint8_t *dones = nullptr, *overtime = nullptr, *tovertime = nullptr;
@@ -148,6 +150,7 @@ struct carlb_env
             s.ballStreams[g] = ballSide ? ballStream[g] : nullptr;
             s.tickStart[g] = tickStart[g];
             s.ballDone[g] = ballDone[g];
+            s.wideDone[g] = phaseOffset ? wideDone[g] : nullptr;
         }
         return s;
     }
@@ -402,10 +405,12 @@ static carlb_status initEnv(carlb_env* p, const carlb_config* cfg)
         // Slices of fewer than ~4k sims would leave the wide stages too small.
         p->groups = std::max(1, std::min(p->groups, cfg->n_sim / 4096));
         if (const char* b = std::getenv("CARLB_BALL_STREAM")) p->ballSide = std::atoi(b) != 0;
+        if (const char* o = std::getenv("CARLB_PHASE_OFFSET")) p->phaseOffset = std::atoi(o) != 0;
         for (int g = 0; g < p->groups; g++)
         {
             ECHECK(p, cudaStreamCreateWithFlags(&p->groupStream[g], cudaStreamNonBlocking));
             ECHECK(p, cudaEventCreateWithFlags(&p->groupJoin[g], cudaEventDisableTiming));
+            ECHECK(p, cudaEventCreateWithFlags(&p->wideDone[g], cudaEventDisableTiming));
             if (p->ballSide)
             {
                 ECHECK(p, cudaStreamCreateWithFlags(&p->ballStream[g], cudaStreamNonBlocking));
@@ -560,6 +565,7 @@ carlb_status carlb_destroy(carlb_env* e)
         if (e->groupStream[g]) cudaStreamDestroy(e->groupStream[g]);
         if (e->tickStart[g]) cudaEventDestroy(e->tickStart[g]);
         if (e->ballDone[g]) cudaEventDestroy(e->ballDone[g]);
+        if (e->wideDone[g]) cudaEventDestroy(e->wideDone[g]);
         if (e->ballStream[g]) cudaStreamDestroy(e->ballStream[g]);
     }
     if (e->evFork) cudaEventDestroy(e->evFork);

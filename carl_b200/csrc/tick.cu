@@ -1838,6 +1838,17 @@ int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch&
             ballKernel<<<ballBlocks, BALL_WARPS * 32, 0, sb>>>(q, a, y, t);
             mark(6, true, sb);
             if (sb != sq && (err = cudaEventRecord((cudaEvent_t)aux.ballDone[g], sb)) != cudaSuccess) return (int)err;
+            // Phase offset between slices: slice g starts its wide stages (flat, ray
+            // finish, suspension) only after the previous slice's wide stages of this
+            // tick (slice 0: the last slice's, previous tick), so one slice's
+            // latency-bound contact / car-car stages overlap another's wide stages.
+            if (nG > 1 && aux.wideDone[0])
+            {
+                const int prev = g == 0 ? nG - 1 : g - 1;
+                if ((g > 0 || t > 0) &&
+                    (err = cudaStreamWaitEvent(sq, (cudaEvent_t)aux.wideDone[prev], 0)) != cudaSuccess)
+                    return (int)err;
+            }
             mark(1, false, sq);
             flatKernel<<<(n + CAND_BLOCK - 1) / CAND_BLOCK, CAND_BLOCK, candSmem, sq>>>(q, a, y, t);
             mark(1, true, sq);
@@ -1847,6 +1858,8 @@ int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch&
             mark(3, false, sq);
             suspKernel<<<(n + SOLVE_BLOCK - 1) / SOLVE_BLOCK, SOLVE_BLOCK, 0, sq>>>(q, a, y, t);
             mark(3, true, sq);
+            if (nG > 1 && aux.wideDone[0] && (err = cudaEventRecord((cudaEvent_t)aux.wideDone[g], sq)) != cudaSuccess)
+                return (int)err;
             mark(4, false, sq);
             contactKernel<<<contactBlocks + meshBlocks, SOLVE_BLOCK, 0, sq>>>(q, a, y, t, contactBlocks);
             mark(4, true, sq);

@@ -88,6 +88,7 @@ struct StageStreams
     void* ballStreams[8]; // optional side stream per slice for the ball's arena stage
     void* tickStart[8];   // event per slice: the previous tick's finish (side stream waits)
     void* ballDone[8];    // event per slice: the ball's arena stage (finish waits)
+    void* wideDone[8];    // optional event per slice: its wide stages of the tick (phase offset)
     void* stageEvents[2 * STAGE_KERNELS];  // optional: start / end events of slice 0's stage
                                            // kernels in the last tick of the launch
 };
