@@ -460,12 +460,13 @@ CB_D void applyRow(Body& b, const Row& r, float impulse)
     b.deltaAng = b.deltaAng + r.angular * impulse;
 }
 
-// Solves one car against its manifold of N points; updates the body's delta /
-// push velocities.  N is a compile-time constant so the rows stay in registers.
+// Solves one car against its manifold of `count` points; updates the body's delta /
+// push velocities.  The row arrays have the compile-time capacity N so they stay in
+// registers; rows at and beyond `count` are skipped, so every lane of a warp runs
+// the same code whatever its contact count.
 template <int N>
-CB_D void solveCarManifoldN(Body& b, const MPoint* p)
+CB_D void solveCarManifoldN(Body& b, const MPoint* p, int count)
 {
-    constexpr int count = N;
     Row normalRow[N], frictionRow[N];
     const V3 centerOffset = b.cen - b.pos;
     const V3 totalVel = b.vel + b.extVel;
@@ -473,8 +474,9 @@ CB_D void solveCarManifoldN(Body& b, const MPoint* p)
     constexpr float invDt = 1.f / PHYS_DT;
 
     #pragma unroll
-    for (int i = 0; i < count; i++)
+    for (int i = 0; i < N; i++)
     {
+        if (i >= count) break;
         const V3 relPos = centerOffset + rotate(b.rot, p[i].carPos);
 
         Row n = axisRow(b, p[i].worldNormal, relPos);
@@ -518,8 +520,9 @@ CB_D void solveCarManifoldN(Body& b, const MPoint* p)
     for (int iter = 0; iter < CAR_SOLVER_ITERS; iter++)
     {
         #pragma unroll
-        for (int i = 0; i < count; i++)
+        for (int i = 0; i < N; i++)
         {
+            if (i >= count) break;
             Row& r = normalRow[i];
             if (r.rhsPen == 0.f) continue;
             const float rv = rowVel(r, b.pushVel, b.turnVel);
@@ -532,15 +535,17 @@ CB_D void solveCarManifoldN(Body& b, const MPoint* p)
     for (int iter = 0; iter < CAR_SOLVER_ITERS; iter++)
     {
         #pragma unroll
-        for (int i = 0; i < count; i++)
+        for (int i = 0; i < N; i++)
         {
+            if (i >= count) break;
             Row& r = normalRow[i];
             const float rv = rowVel(r, b.deltaVel, b.deltaAng);
             applyRow(b, r, solveLowerImpulse(r.rhs, 0.f, r.jacInv, rv, r.lower, r.applied));
         }
         #pragma unroll
-        for (int i = 0; i < count; i++)
+        for (int i = 0; i < N; i++)
         {
+            if (i >= count) break;
             const float maxImpulse = CAR_WORLD_FRICTION * normalRow[i].applied;
             if (maxImpulse <= 0.f) continue;
             Row& f = frictionRow[i];
@@ -554,14 +559,7 @@ CB_D void solveCarManifoldN(Body& b, const MPoint* p)
 
 CB_D void solveCarManifold(Body& b, const MPoint* p, int count)
 {
-    switch (count)
-    {
-    case 1: solveCarManifoldN<1>(b, p); break;
-    case 2: solveCarManifoldN<2>(b, p); break;
-    case 3: solveCarManifoldN<3>(b, p); break;
-    case 4: solveCarManifoldN<4>(b, p); break;
-    default: break;
-    }
+    if (count > 0) solveCarManifoldN<MAX_CAR_MANIFOLD_POINTS>(b, p, count);
 }
 
 CB_D void integrateSplitCorrection(Body& b)

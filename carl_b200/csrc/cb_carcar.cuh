@@ -239,16 +239,17 @@ CB_D void pairApply(Body& a, Body& b, const PairRow& r, float impulse, bool spli
     ab = ab - r.angularB * impulse;
 }
 
-// Two-body solve of N contacts; N is a compile-time constant so the rows stay
-// in registers.
+// Two-body solve of `count` contacts.  The row arrays have the compile-time
+// capacity N so they stay in registers; rows at and beyond `count` are skipped,
+// so every lane of a warp runs the same code whatever its contact count.
 template <int N>
-CB_D void solvePairN(Body& a, Body& b, const CCContact* c)
+CB_D void solvePairN(Body& a, Body& b, const CCContact* c, int count)
 {
-    constexpr int count = N;
     PairRow nr[N], fr[N];
     #pragma unroll
-    for (int i = 0; i < count; i++)
+    for (int i = 0; i < N; i++)
     {
+        if (i >= count) break;
         const V3 relA = a.cen - a.pos + rotate(a.rot, c[i].carPosA);
         const V3 relB = b.cen - b.pos + rotate(b.rot, c[i].carPosB);
 
@@ -274,8 +275,9 @@ CB_D void solvePairN(Body& a, Body& b, const CCContact* c)
     }
     for (int iter = 0; iter < CAR_SOLVER_ITERS; iter++)
         #pragma unroll
-        for (int i = 0; i < count; i++)
+        for (int i = 0; i < N; i++)
         {
+            if (i >= count) break;
             PairRow& r = nr[i];
             const float rv = pairVel(r, a.pushVel, a.turnVel, b.pushVel, b.turnVel);
             pairApply(a, b, r, solveLowerImpulse(r.rhsPen, 0.f, r.jacInv, rv, 0.f, r.appliedPush), true);
@@ -283,15 +285,17 @@ CB_D void solvePairN(Body& a, Body& b, const CCContact* c)
     for (int iter = 0; iter < CAR_SOLVER_ITERS; iter++)
     {
         #pragma unroll
-        for (int i = 0; i < count; i++)
+        for (int i = 0; i < N; i++)
         {
+            if (i >= count) break;
             PairRow& r = nr[i];
             const float rv = pairVel(r, a.deltaVel, a.deltaAng, b.deltaVel, b.deltaAng);
             pairApply(a, b, r, solveLowerImpulse(r.rhs, 0.f, r.jacInv, rv, 0.f, r.applied), false);
         }
         #pragma unroll
-        for (int i = 0; i < count; i++)
+        for (int i = 0; i < N; i++)
         {
+            if (i >= count) break;
             const float maxImpulse = CARCAR_COLLISION_FRICTION * nr[i].applied;
             if (maxImpulse <= 0.f) continue;
             PairRow& f = fr[i];
@@ -303,14 +307,7 @@ CB_D void solvePairN(Body& a, Body& b, const CCContact* c)
 
 CB_D void solvePair(Body& a, Body& b, const CCContact* c, int count)
 {
-    switch (count)
-    {
-    case 1: solvePairN<1>(a, b, c); break;
-    case 2: solvePairN<2>(a, b, c); break;
-    case 3: solvePairN<3>(a, b, c); break;
-    case 4: solvePairN<4>(a, b, c); break;
-    default: break;
-    }
+    if (count > 0) solvePairN<MAX_CAR_MANIFOLD_POINTS>(a, b, c, count);
 }
 
 CB_D void finishPairBody(Body& b)
