@@ -3,6 +3,7 @@
 // reference's host build of the same tables.
 #include "arena.hpp"
 
+#include <algorithm>
 #include <array>
 #include <cmath>
 #include <cstdlib>
@@ -145,6 +146,49 @@ std::string buildArena(const std::string& path, ArenaHost& a)
     a.cellTris.resize(a.cellStart[NUM_CELLS]);
     for (int c = 0; c < NUM_CELLS; c++)
         std::copy(cells[c].begin(), cells[c].end(), a.cellTris.begin() + a.cellStart[c]);
+
+    // Ball grid (see ArenaHost): reach = contact radius + 2 uu of margin, which
+    // covers float rounding in the device's cell lookup.
+    {
+        const double reach = (double)BALL_COLLISION_RADIUS + (double)BALL_ARENA_CONTACT_BREAK + 2.0;
+        const double cell = a.ballCell;
+        double o[3] = { 1e30, 1e30, 1e30 }, e[3] = { -1e30, -1e30, -1e30 };
+        for (int t = 0; t < nTris; t++)
+        {
+            const double l[3] = { lo[t].x, lo[t].y, lo[t].z }, h[3] = { hi[t].x, hi[t].y, hi[t].z };
+            for (int k = 0; k < 3; k++)
+            {
+                o[k] = std::min(o[k], l[k] - reach);
+                e[k] = std::max(e[k], h[k] + reach);
+            }
+        }
+        for (int k = 0; k < 3; k++)
+        {
+            a.ballOrigin[k] = (float)std::floor(o[k]);
+            a.ballDims[k] = (int)std::ceil((e[k] - a.ballOrigin[k]) / cell) + 1;
+        }
+        const size_t nb = (size_t)a.ballDims[0] * a.ballDims[1] * a.ballDims[2];
+        std::vector<std::vector<int32_t>> bcells(nb);
+        for (int t = 0; t < nTris; t++)
+        {
+            const double l[3] = { lo[t].x, lo[t].y, lo[t].z }, h[3] = { hi[t].x, hi[t].y, hi[t].z };
+            int c0[3], c1[3];
+            for (int k = 0; k < 3; k++)
+            {
+                c0[k] = std::max(0, (int)std::floor((l[k] - reach - a.ballOrigin[k]) / cell));
+                c1[k] = std::min(a.ballDims[k] - 1, (int)std::floor((h[k] + reach - a.ballOrigin[k]) / cell));
+            }
+            for (int z = c0[2]; z <= c1[2]; z++)
+                for (int y = c0[1]; y <= c1[1]; y++)
+                    for (int x = c0[0]; x <= c1[0]; x++)
+                        bcells[x + (size_t)a.ballDims[0] * (y + (size_t)a.ballDims[1] * z)].push_back(t);
+        }
+        a.ballCellStart.assign(nb + 1, 0);
+        for (size_t c = 0; c < nb; c++) a.ballCellStart[c + 1] = a.ballCellStart[c] + (int)bcells[c].size();
+        a.ballCellTris.resize(a.ballCellStart[nb]);
+        for (size_t c = 0; c < nb; c++)
+            std::copy(bcells[c].begin(), bcells[c].end(), a.ballCellTris.begin() + a.ballCellStart[c]);
+    }
 
     // Signed dihedral angle across every shared edge.
     a.edgeAngles.assign((size_t)nTris * 3, BOUNDARY_EDGE_ANGLE);

@@ -33,6 +33,16 @@ struct ArenaHost
     std::vector<int32_t> cellTris;  // [cellStart[NUM_CELLS]]
     int32_t maxCellTris = 0;
 
+    // Ball grid: cubic cells of ballCell uu from ballOrigin; a cell lists, in
+    // ascending order, every triangle whose bounding box grown by the ball's
+    // contact reach (plus a margin) overlaps it, so one cell holds every triangle
+    // a ball centred in it can touch.  A ball outside the grid touches nothing.
+    float ballOrigin[3] = { 0.f, 0.f, 0.f };
+    float ballCell = 128.f;
+    int32_t ballDims[3] = { 0, 0, 0 };
+    std::vector<int32_t> ballCellStart;  // [ballDims product + 1]
+    std::vector<int32_t> ballCellTris;   // [ballCellStart.back()]
+
     int nVerts() const { return (int)verts.size() / 3; }
     int nTris() const { return (int)tris.size() / 3; }
 };

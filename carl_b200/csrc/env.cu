@@ -80,6 +80,11 @@ struct carlb_env
     float4* triAng = nullptr;
     float4* cellSph = nullptr;
     float4* cellV = nullptr;
+    float4 ballGrid{};
+    int ballDims[3] = { 0, 0, 0 };
+    int* ballCellStart = nullptr;
+    int* ballCellTris = nullptr;
+    float4* ballCellSph = nullptr;
     float carReach = 0.f;
     int* cellStart = nullptr;
     int* cellTris = nullptr;
@@ -154,7 +159,8 @@ struct carlb_env
         }
         return s;
     }
-    ArenaDev arena() const { return ArenaDev{ triV, triAng, cellStart, cellTris, hitWords, cellSph, carReach, cellV }; }
+    ArenaDev arena() const { return ArenaDev{ triV, triAng, cellStart, cellTris, hitWords, cellSph, carReach, cellV, ballGrid, ballDims[0], ballDims[1],
+                         ballDims[2], ballCellStart, ballCellTris, ballCellSph }; }
     Outputs outputs() const
     {
         return Outputs{ rewards, dones, scoreDiff, episodeTicks, tScoreDiff, tEpisodeTicks, overtime, tovertime };
@@ -498,6 +504,22 @@ static carlb_status initEnv(carlb_env* p, const carlb_config* cfg)
     ECHECK(p, allocZero(p, &p->cellV, cellV.size()));
     ECHECK(p, cudaMemcpyAsync(p->cellV, cellV.data(), cellV.size() * sizeof(float4), cudaMemcpyHostToDevice,
                               p->stream));
+    {
+        std::vector<float4> bsph(host->ballCellTris.size());
+        for (size_t k = 0; k < bsph.size(); k++) bsph[k] = triSph[host->ballCellTris[k]];
+        p->ballGrid = make_float4(host->ballOrigin[0], host->ballOrigin[1], host->ballOrigin[2], 1.f / host->ballCell);
+        for (int k = 0; k < 3; k++) p->ballDims[k] = host->ballDims[k];
+        ECHECK(p, allocZero(p, &p->ballCellStart, host->ballCellStart.size()));
+        ECHECK(p, allocZero(p, &p->ballCellTris, std::max<size_t>(1, host->ballCellTris.size())));
+        ECHECK(p, allocZero(p, &p->ballCellSph, std::max<size_t>(1, bsph.size())));
+        ECHECK(p, cudaMemcpyAsync(p->ballCellStart, host->ballCellStart.data(), host->ballCellStart.size() * 4,
+                                  cudaMemcpyHostToDevice, p->stream));
+        ECHECK(p, cudaMemcpyAsync(p->ballCellTris, host->ballCellTris.data(), host->ballCellTris.size() * 4,
+                                  cudaMemcpyHostToDevice, p->stream));
+        ECHECK(p, cudaMemcpyAsync(p->ballCellSph, bsph.data(), bsph.size() * sizeof(float4), cudaMemcpyHostToDevice,
+                                  p->stream));
+        ECHECK(p, cudaStreamSynchronize(p->stream));  // the host vectors go out of scope
+    }
     ECHECK(p, allocZero(p, &p->cellSph, cellSph.size()));
     ECHECK(p, cudaMemcpyAsync(p->cellSph, cellSph.data(), cellSph.size() * sizeof(float4), cudaMemcpyHostToDevice,
                               p->stream));

@@ -182,39 +182,38 @@ __device__ V3 ballArenaSolve(const SmemSoa& cars, const SmemSoa& sims, int s, in
     const V3 velNoExt = b.velNoExt;
     const V3 exportedPos = b.exportedPos;
     V3 pushVel = v3zero();
-    // Arena triangles of the grid cells around the ball, tested across lanes.
+    // Arena triangles of the ball-grid cell holding the ball centre (it lists every
+    // triangle within the contact reach of any point of the cell), tested across lanes.
     const V3 center = exportedPos;
-    const V3 ext = v3fill(BALL_COLLISION_RADIUS + BALL_ARENA_CONTACT_BREAK);
-    const I3 lo = gridCell(center - ext);
-    const I3 hi = gridCell(center + ext);
-    const int nx = hi.x - lo.x + 1, ny = hi.y - lo.y + 1, nz = hi.z - lo.z + 1;
-    const int nCells = nx * ny * nz;
+    const float4 g = arena.ballGrid;
+    const float fx = (center.x - g.x) * g.w, fy = (center.y - g.y) * g.w, fz = (center.z - g.z) * g.w;
+    int start = 0, end = 0;
+    if (fx >= 0.f && fx < (float)arena.ballDimX && fy >= 0.f && fy < (float)arena.ballDimY && fz >= 0.f &&
+        fz < (float)arena.ballDimZ)
+    {
+        const int c = (int)fx + arena.ballDimX * ((int)fy + arena.ballDimY * (int)fz);
+        start = __ldg(&arena.ballCellStart[c]);
+        end = __ldg(&arena.ballCellStart[c + 1]);
+    }
     int& hitCount = wbuf[WARP_HIT_BUF];
     if (lane == 0) hitCount = 0;
     __syncwarp();
-    for (int q = 0; q < nCells; q++)
+    for (int e = start + lane; e < end; e += 32)
     {
-        const int x = lo.x + q % nx, y = lo.y + (q / nx) % ny, z = lo.z + q / (nx * ny);
-        const int cell = flatCell(I3{ x, y, z });
-        const int start = __ldg(&arena.cellStart[cell]);
-        const int end = __ldg(&arena.cellStart[cell + 1]);
-        for (int e = start + lane; e < end; e += 32)
+        // A triangle beyond the contact radius (plus 1 uu) cannot touch the ball.
+        const float4 sph = __ldg(&arena.ballCellSph[e]);
+        const float dx = sph.x - center.x, dy = sph.y - center.y, dz = sph.z - center.z;
+        const float rr = sph.w + (BALL_COLLISION_RADIUS + BALL_ARENA_CONTACT_BREAK + 1.f);
+        if (dx * dx + dy * dy + dz * dz > rr * rr) continue;
+        const int tri = __ldg(&arena.ballCellTris[e]);
+        V3 v0, v1, v2;
+        int flags;
+        loadTri(arena, tri, v0, v1, v2, flags);
+        BallContact c;
+        if (sphereTriangle(center, BALL_COLLISION_RADIUS, v0, v1, v2, c))
         {
-            // A triangle beyond the contact radius (plus 1 uu) cannot touch the ball.
-            const float4 sph = __ldg(&arena.cellSph[e]);
-            const float dx = sph.x - center.x, dy = sph.y - center.y, dz = sph.z - center.z;
-            const float rr = sph.w + (BALL_COLLISION_RADIUS + BALL_ARENA_CONTACT_BREAK + 1.f);
-            if (dx * dx + dy * dy + dz * dz > rr * rr) continue;
-            const int tri = __ldg(&arena.cellTris[e]);
-            V3 v0, v1, v2;
-            int flags;
-            loadTri(arena, tri, v0, v1, v2, flags);
-            BallContact c;
-            if (sphereTriangle(center, BALL_COLLISION_RADIUS, v0, v1, v2, c))
-            {
-                const int slot = atomicAdd(&hitCount, 1);
-                if (slot < WARP_HIT_BUF) wbuf[slot] = tri;
-            }
+            const int slot = atomicAdd(&hitCount, 1);
+            if (slot < WARP_HIT_BUF) wbuf[slot] = tri;
         }
     }
     __syncwarp();
@@ -226,8 +225,8 @@ __device__ V3 ballArenaSolve(const SmemSoa& cars, const SmemSoa& sims, int s, in
         const int n = hitCount;
         if (n <= WARP_HIT_BUF)
         {
-            // Ascending, de-duplicated triangle order (the reference merges the
-            // per-cell lists in triangle order and skips repeats).
+            // Ascending triangle order (the reference merges the per-cell lists in
+            // triangle order; the ball cell's list has no repeats).
             for (int i = 1; i < n; i++)
             {
                 const int v = wbuf[i];
@@ -239,12 +238,9 @@ __device__ V3 ballArenaSolve(const SmemSoa& cars, const SmemSoa& sims, int s, in
                 }
                 wbuf[j + 1] = v;
             }
-            int last = -1;
             for (int i = 0; i < n; i++)
             {
                 const int tri = wbuf[i];
-                if (tri == last) continue;
-                last = tri;
                 V3 v0, v1, v2;
                 int flags;
                 loadTri(arena, tri, v0, v1, v2, flags);
@@ -255,34 +251,16 @@ __device__ V3 ballArenaSolve(const SmemSoa& cars, const SmemSoa& sims, int s, in
         }
         else
         {
-            // Too many hits to buffer: walk the union of the cell lists in
-            // ascending triangle order directly.
-            int cursor = -1;
-            while (true)
+            // Too many hits to buffer: walk the (ascending) cell list directly.
+            for (int e = start; e < end; e++)
             {
-                int next = 0x7fffffff;
-                for (int q = 0; q < nCells; q++)
-                {
-                    const int x = lo.x + q % nx, y = lo.y + (q / nx) % ny, z = lo.z + q / (nx * ny);
-                    const int cell = flatCell(I3{ x, y, z });
-                    for (int e = __ldg(&arena.cellStart[cell]); e < __ldg(&arena.cellStart[cell + 1]); e++)
-                    {
-                        const int tri = __ldg(&arena.cellTris[e]);
-                        if (tri > cursor)
-                        {
-                            if (tri < next) next = tri;
-                            break;  // cell lists are ascending
-                        }
-                    }
-                }
-                if (next == 0x7fffffff) break;
-                cursor = next;
+                const int tri = __ldg(&arena.ballCellTris[e]);
                 V3 v0, v1, v2;
                 int flags;
-                loadTri(arena, next, v0, v1, v2, flags);
+                loadTri(arena, tri, v0, v1, v2, flags);
                 BallContact c;
                 if (sphereTriangle(center, BALL_COLLISION_RADIUS, v0, v1, v2, c))
-                    insertBallContact(set, count, c, center, v0, v1, v2, triAngles(arena, next));
+                    insertBallContact(set, count, c, center, v0, v1, v2, triAngles(arena, tri));
             }
         }
 

@@ -21,6 +21,13 @@ struct ArenaDev
                             // radius rounded up
     float carReach;         // radius around a car's box centre that holds its box and wheel rays, plus margin
     const float4* cellV;    // [3 * cellStart[NUM_CELLS]]: vertices of cellTris[e] (flags in vertex 0's w)
+    // Ball grid (ArenaHost::ball*): origin xyz and 1 / cell size in w, dimensions,
+    // per-cell triangle lists and the bounding sphere of each list entry.
+    float4 ballGrid;
+    int ballDimX, ballDimY, ballDimZ;
+    const int* ballCellStart;
+    const int* ballCellTris;
+    const float4* ballCellSph;
 };
 
 struct TickParams

@@ -592,3 +592,26 @@ extern "C" int hosttick_kickoff_table(void* h, int* out)
         for (int k = 0; k < 4; k++) out[4 * r + k] = e->T.kickoffPerm[r][k];
     return 0;
 }
+
+// Product ball grid (carl_b200/csrc/arena.cpp) for the ball-grid coverage test:
+// geom = {origin x, y, z, cell size}, dims = {x, y, z, entries}.
+extern "C" int hosttick_ball_grid(void* h, float* geom, int* dims)
+{
+    auto* e = static_cast<HostEnv*>(h);
+    for (int k = 0; k < 3; k++)
+    {
+        geom[k] = e->arena.ballOrigin[k];
+        dims[k] = e->arena.ballDims[k];
+    }
+    geom[3] = e->arena.ballCell;
+    dims[3] = (int)e->arena.ballCellTris.size();
+    return 0;
+}
+
+extern "C" int hosttick_ball_lists(void* h, int* start, int* tris)
+{
+    auto* e = static_cast<HostEnv*>(h);
+    std::memcpy(start, e->arena.ballCellStart.data(), e->arena.ballCellStart.size() * 4);
+    std::memcpy(tris, e->arena.ballCellTris.data(), e->arena.ballCellTris.size() * 4);
+    return 0;
+}

@@ -48,6 +48,8 @@ def _load():
         lib.hosttick_arena_sizes.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
         lib.hosttick_arena_tables.argtypes = [ctypes.c_void_p] * 8
         lib.hosttick_kickoff_table.argtypes = [ctypes.c_void_p] * 2
+        lib.hosttick_ball_grid.argtypes = [ctypes.c_void_p] * 3
+        lib.hosttick_ball_lists.argtypes = [ctypes.c_void_p] * 3
         _lib = lib
     return _lib
 
@@ -107,6 +109,17 @@ class HostTick:
                                                  ("verts", "tris", "prefix", "tri_idx", "edge_angles", "normals",
                                                   "flags")])
         return out
+
+    def ball_grid(self):
+        """(origin[3], cell size, dims[3], cell starts, cell triangle lists) of the product's ball grid."""
+        geom = np.zeros(4, np.float32)
+        dims = np.zeros(4, np.int32)
+        self.lib.hosttick_ball_grid(self.h, geom.ctypes.data, dims.ctypes.data)
+        n = int(dims[0]) * int(dims[1]) * int(dims[2])
+        start = np.zeros(n + 1, np.int32)
+        tris = np.zeros(max(1, int(dims[3])), np.int32)
+        self.lib.hosttick_ball_lists(self.h, start.ctypes.data, tris.ctypes.data)
+        return geom[:3], float(geom[3]), dims[:3], start, tris
 
     def kickoff_table(self) -> np.ndarray:
         out = np.zeros((120, 4), dtype=np.int32)
