@@ -499,6 +499,45 @@ CB_D int solveCarCarPair(const SimCars<S>& sc, int ia, int ib)
 
 // Distance gate of a pair (the only test that needs no state update).
 template <class S>
+CB_D bool carCarGate(const S& c, int A, int B);
+
+// All pairs of one sim in the reference's order (a < b, pair solved as (b, a)).
+// Each call first skips to the sim's next pair within reach, so threads of a warp
+// that step different sims run their (expensive) pair solves together instead of
+// waiting on each other's out-of-reach pairs; the pairs a sim solves, and their
+// order, are the sequential ones (solveCarCarPair re-checks the gate itself).
+// kept[pair] receives the manifold point count of every pair (0 when skipped).
+template <class S>
+CB_D void solveCarCarSim(const SimCars<S>& sc, int* kept, int maxKept)
+{
+    const int nCars = sc.nCars;
+    const int nPairs = nCars * (nCars - 1) / 2;
+    for (int q = 0; q < nPairs && q < maxKept; q++) kept[q] = 0;
+    int a = 0, b = 1, pair = 0;
+    while (pair < nPairs)
+    {
+        while (pair < nPairs && !carCarGate(sc.cars, sc.base + b, sc.base + a))
+        {
+            pair++;
+            if (++b == nCars)
+            {
+                a++;
+                b = a + 1;
+            }
+        }
+        if (pair >= nPairs) break;
+        const int k = solveCarCarPair(sc, b, a);
+        if (pair < maxKept) kept[pair] = k;
+        pair++;
+        if (++b == nCars)
+        {
+            a++;
+            b = a + 1;
+        }
+    }
+}
+
+template <class S>
 CB_D bool carCarGate(const S& c, int A, int B)
 {
     if (c.n(C_DEMOED, A) || c.n(C_DEMOED, B)) return false;

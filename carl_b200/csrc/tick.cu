@@ -1527,13 +1527,11 @@ __global__ void __launch_bounds__(CC_BLOCK) carCarKernel(TickParams p, int t)
     const int sIdx = activeS[tid];
     const int sb = sIdx * nCars;
     SimCars<CarSoa> sc{ cars, sb, nCars, p.nBlue, (int)(p.globalCarBase + sb), tick, p.seed };
-    int pair = 0;
-    for (int a = 0; a < nCars - 1; a++)
-        for (int b = a + 1; b < nCars; b++, pair++)
-        {
-            const int kept = solveCarCarPair(sc, b, a);
-            if (lastTick && p.diagSim && pair < DIAG_SIM_WORDS) p.diagSim[pair * p.simStride + sIdx] = kept;
-        }
+    int kept[DIAG_SIM_WORDS];
+    const bool diag = lastTick && p.diagSim;
+    solveCarCarSim(sc, kept, diag ? DIAG_SIM_WORDS : 0);
+    if (diag)
+        for (int q = 0; q < nPairs && q < DIAG_SIM_WORDS; q++) p.diagSim[q * p.simStride + sIdx] = kept[q];
 }
 
 // Ball stage prelude, one thread per sim: hand-over values for every sim and the
