@@ -106,6 +106,13 @@ struct carlb_env
     cudaEvent_t tickStart[8] = {}, ballDone[8] = {};
     bool phaseOffset = true;  // slices alternate their wide stages (CARLB_PHASE_OFFSET=0 disables)
     cudaEvent_t wideDone[8] = {};
+    // Staged launches replayed from instantiated graphs (CARLB_GRAPH=0 disables): one per
+    // (action kind, tick count, diagnostics, stage timing); the tick count before
+    // each launch is written to tickDev, which the captured stage kernels read.
+    bool useGraph = true;
+    int* tickDev = nullptr;
+    struct TickGraph { int kind, nTicks; bool diag, timing; cudaGraphExec_t exec; };
+    std::vector<TickGraph> graphs;
 
     float *obs = nullptr, *tobs = nullptr, *packed = nullptr, *tpacked = nullptr, *rewards = nullptr;
     uint8_t *dones = nullptr, *overtime = nullptr, *tovertime = nullptr;
@@ -234,6 +241,45 @@ carlb_status launchTicks(carlb_env* e, carlb_action_kind kind, int nTicks)
     p.nTicks = nTicks;
     p.tileSims = e->tileSims;
     p.compatFlags = e->cfg.compat_flags;
+    if (e->staged && e->useGraph && nTicks > 0)
+    {
+        cudaGraphExec_t exec = nullptr;
+        for (const auto& g : e->graphs)
+            if (g.kind == (int)kind && g.nTicks == nTicks && g.diag == e->diagnostics && g.timing == e->stageTiming)
+                exec = g.exec;
+        if (!exec && e->graphs.size() < 16)
+        {
+            // Capture the launch once; every replay reads the tick count from tickDev.
+            const int serr = stagedSetup();
+            if (serr) return cudaFail(e, (cudaError_t)serr, "staged tick setup");
+            TickParams q = p;
+            q.tickDev = e->tickDev;
+            ECHECK(e, cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+            const int lerr = launchTickStaged(q, e->arena(), e->scratch, e->stream, e->stageStreams());
+            cudaGraph_t graph = nullptr;
+            const cudaError_t cerr = cudaStreamEndCapture(e->stream, &graph);
+            if (lerr || cerr != cudaSuccess)
+            {
+                if (graph) cudaGraphDestroy(graph);
+                return cudaFail(e, lerr ? (cudaError_t)lerr : cerr, "tick graph capture");
+            }
+            const cudaError_t ierr = cudaGraphInstantiate(&exec, graph, 0);
+            cudaGraphDestroy(graph);
+            if (ierr != cudaSuccess) return cudaFail(e, ierr, "tick graph instantiate");
+            e->graphs.push_back({ (int)kind, nTicks, e->diagnostics, e->stageTiming, exec });
+        }
+        if (exec)
+        {
+            ECHECK(e, cudaEventRecord(e->ev0, e->stream));
+            const int serr = launchSetTick(e->tickDev, e->tick, e->stream);
+            if (serr) return cudaFail(e, (cudaError_t)serr, "tick counter");
+            ECHECK(e, cudaGraphLaunch(exec, e->stream));
+            e->stageTimed = e->stageTiming;
+            ECHECK(e, cudaEventRecord(e->ev1, e->stream));
+            e->tick += nTicks;
+            return CARLB_OK;
+        }
+    }
     ECHECK(e, cudaEventRecord(e->ev0, e->stream));
     const int err = e->staged
         ? launchTickStaged(p, e->arena(), e->scratch, e->stream, e->stageStreams())
@@ -412,6 +458,8 @@ static carlb_status initEnv(carlb_env* p, const carlb_config* cfg)
         p->groups = std::max(1, std::min(p->groups, cfg->n_sim / 4096));
         if (const char* b = std::getenv("CARLB_BALL_STREAM")) p->ballSide = std::atoi(b) != 0;
         if (const char* o = std::getenv("CARLB_PHASE_OFFSET")) p->phaseOffset = std::atoi(o) != 0;
+        if (const char* gr = std::getenv("CARLB_GRAPH")) p->useGraph = std::atoi(gr) != 0;
+        if (p->useGraph) ECHECK(p, allocZero(p, &p->tickDev, (size_t)1));
         for (int g = 0; g < p->groups; g++)
         {
             ECHECK(p, cudaStreamCreateWithFlags(&p->groupStream[g], cudaStreamNonBlocking));
@@ -578,6 +626,7 @@ carlb_status carlb_destroy(carlb_env* e)
         if (e->groupStream[g]) cudaStreamSynchronize(e->groupStream[g]);
         if (e->ballStream[g]) cudaStreamSynchronize(e->ballStream[g]);
     }
+    for (const auto& g : e->graphs) cudaGraphExecDestroy(g.exec);
     for (void* v : e->allocations) cudaFree(v);
     if (e->ev0) cudaEventDestroy(e->ev0);
     if (e->ev1) cudaEventDestroy(e->ev1);

@@ -914,6 +914,11 @@ __global__ void __launch_bounds__(256) tickKernel(TickParams p, ArenaDev arena)
 //   finishKernel   ball vs cars + integration + goal, car integration + finish, boost pads
 // =========================================================================================
 
+// Tick count before the first tick of the launch (device counter when set).
+__device__ __forceinline__ int tickBase(const TickParams& p) { return p.tickDev ? *p.tickDev : p.tick0; }
+
+__global__ void setTickKernel(int* dst, int value) { *dst = value; }
+
 constexpr int CAND_BLOCK = 128;   // cars per candKernel CTA (car numbers fit the uint8 item map)
 constexpr int CAND_MAP_CAP = 12288;  // items per CTA resolved through the shared item -> car map
 constexpr int RAY_BLOCK = 128;    // cars per rayCtlKernel CTA
@@ -1274,7 +1279,7 @@ __global__ void __launch_bounds__(SOLVE_BLOCK) suspKernel(TickParams p, ArenaDev
     const int i = blockIdx.x * SOLVE_BLOCK + threadIdx.x;
     if (i >= n) return;
     const CarSoa cars{ p.car, (int)p.carStride };
-    const int tick = p.tick0 + t + 1;
+    const int tick = tickBase(p) + t + 1;
     const bool lastTick = t == p.nTicks - 1;
     const int HW = arena.hitWords;
     const int cellFirst = x.first[i];
@@ -1507,7 +1512,7 @@ __global__ void __launch_bounds__(CC_BLOCK) carCarKernel(TickParams p, int t)
     const int s = blockIdx.x * CC_BLOCK + tid;
     const CarSoa cars{ p.car, (int)p.carStride };
     const int nCars = p.nCars;
-    const int tick = p.tick0 + t + 1;
+    const int tick = tickBase(p) + t + 1;
     const bool lastTick = t == p.nTicks - 1;
     const int nPairs = nCars * (nCars - 1) / 2;
     if (tid == 0) nActive = 0;
@@ -1565,7 +1570,7 @@ __global__ void __launch_bounds__(BALL_WARPS * 32) ballKernel(TickParams p, Aren
         b.posBT = loadBallScratch(x.ball, stride, s, 1);
         b.preSolveBT = loadBallScratch(x.ball, stride, s, 2);
         b.velNoExt = loadBallScratch(x.ball, stride, s, 4);
-        const V3 pushVel = ballArenaSolve(cars, sims, s, p.nCars, p.tick0 + t + 1, arena, wbufS[warp], lane, b);
+        const V3 pushVel = ballArenaSolve(cars, sims, s, p.nCars, tickBase(p) + t + 1, arena, wbufS[warp], lane, b);
         if (lane == 0) storeBallScratch(x.ball, stride, s, &pushVel, 3, 1);
         __syncwarp();
     }
@@ -1580,7 +1585,7 @@ __global__ void __launch_bounds__(FIN_THREADS) finishKernel(TickParams p, StageS
     const int carsHere = simsHere * nCars;
     const CarSoa cars{ p.car, (int)p.carStride };
     const CarSoa sims{ p.sim, (int)p.simStride };
-    const int tick = p.tick0 + t + 1;
+    const int tick = tickBase(p) + t + 1;
     const bool lastTick = t == p.nTicks - 1;
 
     if (blockIdx.x == 0 && tid == 0)
@@ -1710,6 +1715,29 @@ size_t stageCandSmemBytes(int hitWords)
     return bytes + 8 * 4 * (size_t)B + CAND_MAP_CAP;
 }
 
+int stagedSetup()
+{
+    static std::mutex lock;
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return (int)err;
+    std::lock_guard<std::mutex> guard(lock);
+    if (dev < 0 || dev >= 64 || !configured[dev])
+    {
+        err = cudaFuncSetAttribute(flatKernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+        if (err != cudaSuccess) return (int)err;
+        if (dev >= 0 && dev < 64) configured[dev] = true;
+    }
+    return 0;
+}
+
+int launchSetTick(int* dst, int value, void* stream)
+{
+    setTickKernel<<<1, 1, 0, (cudaStream_t)stream>>>(dst, value);
+    return (int)cudaGetLastError();
+}
+
 int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch& x, void* stream,
                      const StageStreams& aux)
 {
@@ -1718,16 +1746,9 @@ int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch&
         return (int)cudaErrorInvalidValue;
     cudaStream_t st = (cudaStream_t)stream;
     const size_t candSmem = stageCandSmemBytes(a.hitWords);
-    static bool configured[64] = {};
+    if (const int e = stagedSetup()) return e;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64 || !configured[dev])
-    {
-        const cudaError_t err = cudaFuncSetAttribute(flatKernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                     64 * 1024);
-        if (err != cudaSuccess) return (int)err;
-        if (dev >= 0 && dev < 64) configured[dev] = true;
-    }
     if (candSmem > 64 * 1024) return (int)cudaErrorInvalidValue;
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -1795,8 +1816,15 @@ int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch&
             const bool timed = g == 0 && t == p.nTicks - 1 && aux.stageEvents[0];
             // Events around stage k: stageEvents[2k] (start), [2k + 1] (end), on the
             // stream the stage kernel runs on.
+            // Under stream capture the record becomes an event node of the graph
+            // (a plain record there is only an ordering edge).
             auto mark = [&](int k, bool end, cudaStream_t on) {
-                if (timed) cudaEventRecord((cudaEvent_t)aux.stageEvents[2 * k + (end ? 1 : 0)], on);
+                if (!timed) return;
+                cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+                cudaStreamIsCapturing(on, &cs);
+                cudaEventRecordWithFlags((cudaEvent_t)aux.stageEvents[2 * k + (end ? 1 : 0)], on,
+                                         cs == cudaStreamCaptureStatusActive ? cudaEventRecordExternal
+                                                                             : cudaEventRecordDefault);
             };
             // The ball's arena stage reads only the ball and the cars' last-hit ticks,
             // which no car stage of this tick writes before the finish kernel, so with

@@ -43,6 +43,8 @@ struct TickParams
     int actionKind;
     int nSim, nCars, nBlue, seed;
     int tick0;              // tick count before the first tick of this launch
+    const int* tickDev;     // staged path: when set, the tick count is read from here instead
+                            // (lets a captured graph of the launch be replayed at any tick)
     int nTicks;
     int tileSims;           // sims per CTA
     int compatFlags;        // carlb_config::compat_flags
@@ -104,6 +106,12 @@ struct StageStreams
 constexpr size_t STATIC_SCRATCH_BYTES = 64ull << 20;
 // Device address of that scratch on the current device (looked up once per device).
 int staticScratchAddress(void** ptr, size_t* bytes);
+
+// One-time per-device setup of the staged kernels (shared-memory opt-in); call
+// before capturing a launch into a graph.
+int stagedSetup();
+// Writes `value` to the device tick counter `dst` on `stream`.
+int launchSetTick(int* dst, int value, void* stream);
 
 // The same ticks as a sequence of stage kernels over the state in global memory.
 int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch& x, void* stream,
