@@ -241,7 +241,10 @@ carlb_status launchTicks(carlb_env* e, carlb_action_kind kind, int nTicks)
     p.nTicks = nTicks;
     p.tileSims = e->tileSims;
     p.compatFlags = e->cfg.compat_flags;
-    if (e->staged && e->useGraph && nTicks > 0)
+    // A caller capturing the env stream into its own graph gets the kernels in that capture.
+    cudaStreamCaptureStatus outer = cudaStreamCaptureStatusNone;
+    ECHECK(e, cudaStreamIsCapturing(e->stream, &outer));
+    if (e->staged && e->useGraph && nTicks > 0 && outer == cudaStreamCaptureStatusNone)
     {
         cudaGraphExec_t exec = nullptr;
         for (const auto& g : e->graphs)
