@@ -84,6 +84,10 @@ def parse_args():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--workload", choices=["c3", "step", "reset"], default="c3",
+                    help="c3: the headline tick throughput; step: env steps at frameskip 8 (ticks + packing); "
+                         "reset: env steps with masked resets (C5 shard)")
+    ap.add_argument("--reset-n-sim", type=int, default=131072, help="sims of the reset workload (4v4)")
     return ap.parse_args()
 
 
@@ -453,11 +457,147 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     env.close()
 
 
+RESET_FRACTION = 0.01
+
+
+def kickoff_rows(n_sim: int, nb: int, no: int, seed: int) -> dict:
+    """apply_reset_state inputs, one row per sim, holding each sim's kickoff state."""
+    from carl_b200 import capi
+
+    n_cars = nb + no
+    env = capi.Env(n_sim, nb, no, seed)
+    env.reset()
+    f = lambda name: env.read_field(name).view(np.float32)  # noqa: E731
+    rows = {
+        "ball_position": f("BALL_POS").reshape(n_sim, 3), "ball_velocity": f("BALL_VEL").reshape(n_sim, 3),
+        "ball_angular_velocity": f("BALL_ANG").reshape(n_sim, 3),
+        "car_position": f("CAR_POS").reshape(n_sim, n_cars, 3), "car_rotation": f("CAR_ROT").reshape(n_sim, n_cars, 4),
+        "car_velocity": f("CAR_VEL").reshape(n_sim, n_cars, 3),
+        "car_angular_velocity": f("CAR_ANG").reshape(n_sim, n_cars, 3),
+        "car_demoed": env.read_field("CAR_IS_DEMOED").reshape(n_sim, n_cars).astype(np.uint8),
+        "blue_score": np.zeros(n_sim, np.int32), "orange_score": np.zeros(n_sim, np.int32),
+        "episode_ticks": np.zeros(n_sim, np.int32),
+    }
+    env.close()
+    return {k: np.ascontiguousarray(v) for k, v in rows.items()}
+
+
+def run_env_workload(args, resets: bool) -> None:
+    """The env step path (python/carl.cu:312-370: frameskip ticks, then reward /
+    done / transition packing, auto-reset and obs / state packing), timed with
+    CUDA events on the env stream, beside the same sequence on the reference's
+    own CUDA build (`carlrefgpu_time_reset_steps`).
+
+    step:  config C3 (3v3, n_sim sims, seeded floor states), frameskip 8 (the
+           gymnasium wrapper's default), discrete actions; env-steps/s.
+    reset: config C5's per-GPU shard (4v4, --reset-n-sim sims, C4 mixed states),
+           frameskip 1, each env step followed by a masked apply_reset_state
+           that puts a random 1 % of the sims back to their kickoff state; the
+           fused reset kernel, the separate part kernels (CARLB_FUSED_RESET=0)
+           and the reference run the same sequence, step and reset timed apart."""
+    import torch
+
+    from carl_b200 import capi, workloads
+
+    if resets:
+        nb = no = 4
+        n_sim, frameskip = args.reset_n_sim, 1
+    else:
+        nb, no = args.blue, args.orange
+        n_sim, frameskip = args.n_sim, TICKS_PER_STEP
+    n_cars = nb + no
+    rng = np.random.default_rng(args.seed + 5)
+    rows = kickoff_rows(n_sim, nb, no, args.seed) if resets else None
+    n_steps = args.warmup + args.steps
+    masks = (rng.uniform(size=(n_steps, n_sim)) < RESET_FRACTION).astype(np.uint8) if resets else None
+    actions = workloads.discrete_actions(rng, n_sim * n_cars).reshape(n_sim, n_cars, 7)
+    order = ["ball_position", "ball_velocity", "ball_angular_velocity", "car_position", "car_rotation",
+             "car_velocity", "car_angular_velocity", "car_demoed"]
+    results = {}
+    snap = None
+    for mode in (("fused", "parts") if resets else ("b200",)):
+        os.environ["CARLB_FUSED_RESET"] = "0" if mode == "parts" else "1"
+        env = capi.Env(n_sim, nb, no, args.seed, frameskip=frameskip)
+        if snap is None:
+            (workloads.mixed_state if resets else workloads.floor_state)(env, args.seed)
+            snap = env.snapshot()
+        else:
+            env.restore(snap)
+        stream = torch.cuda.ExternalStream(env.stream)
+        dev = {k: torch.from_numpy(v).cuda() for k, v in rows.items()} if resets else {}
+        dmask = torch.from_numpy(masks).cuda() if resets else None
+        act = torch.from_numpy(actions).cuda()
+        torch.cuda.synchronize()
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+        for i in range(n_steps):
+            timed = i >= args.warmup
+            e = ev[i - args.warmup] if timed else None
+            if timed:
+                e[0].record(stream)
+            env.env_step(capi.ACTIONS_DISCRETE, act)
+            if timed:
+                e[1].record(stream)
+            if resets:
+                env.apply_reset_state(n_sim, *[dev[o] for o in order], True, None, None, dev["blue_score"],
+                                      dev["orange_score"], dev["episode_ticks"], reset_mask=dmask[i])
+            if timed:
+                e[2].record(stream)
+        env.synchronize()
+        step_ms = sum(a.elapsed_time(b) for a, b, _ in ev) / args.steps
+        reset_ms = sum(b.elapsed_time(c) for _, b, c in ev) / args.steps
+        results[mode] = {"step_ms": step_ms, "reset_ms": reset_ms}
+        env.close()
+    os.environ.pop("CARLB_FUSED_RESET", None)
+    try:
+        from oracle.refenv import RefGpu
+
+        ref = RefGpu(n_sim, nb, no, args.seed, frameskip=frameskip)
+        ref.restore(snap)
+        if args.warmup:
+            ref.time_reset_steps(capi.ACTIONS_DISCRETE, actions, args.warmup, rows,
+                                 masks[: args.warmup] if resets else None)
+        s_ms, r_ms = ref.time_reset_steps(capi.ACTIONS_DISCRETE, actions, args.steps, rows,
+                                          masks[args.warmup:] if resets else None)
+        ref.close()
+        results["reference_cuda_build"] = {"step_ms": s_ms / args.steps, "reset_ms": r_ms / args.steps}
+    except Exception as exc:  # the reference build is optional here
+        results["reference_cuda_build"] = {"unavailable": str(exc)}
+    for r in results.values():
+        if "step_ms" in r:
+            ms = r["step_ms"] + r["reset_ms"]
+            r["agent_steps_per_s"] = n_sim * n_cars * frameskip / (ms / 1e3)
+            r["env_steps_per_s"] = n_sim / (ms / 1e3)
+    ours = results["fused" if resets else "b200"]
+    if resets:
+        metric = "agent-steps/sec, env steps with 1% masked resets per step"
+        workload = (f"C5 per-GPU shard: 4v4 n_sim={n_sim}, frameskip 1, env_step + masked apply_reset_state "
+                    f"of {RESET_FRACTION:.0%} of sims per step")
+        data = "synthetic (seeded C4 mixed states, discrete actions, random 1% masks, kickoff reset rows)"
+    else:
+        metric = f"env-steps/sec at {nb}v{no} n_sim={n_sim}, frameskip {frameskip}"
+        workload = f"C3 {nb}v{no} n_sim={n_sim}, env_step (frameskip {frameskip} ticks + packing), discrete actions"
+        data = "synthetic (seeded C3 floor states, discrete actions)"
+    line = {
+        "metric": metric, "value": ours["agent_steps_per_s"] if resets else ours["env_steps_per_s"],
+        "unit": UNIT if resets else "env-steps/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ours["step_ms"] + ours["reset_ms"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": data, "config": {"workload": workload},
+        "modes": results,
+    }
+    if resets:
+        line["gpu_launches_per_reset"] = {"fused": 1, "parts": 8}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.workload in ("reset", "step"):
+        if rank == 0:
+            run_env_workload(args, resets=args.workload == "reset")
+        return
     if args.impl == "reference":
         run_reference(args, rank, world)
         return

@@ -110,6 +110,10 @@ struct carlb_env
     // (action kind, tick count, diagnostics, stage timing); the tick count before
     // each launch is written to tickDev, which the captured stage kernels read.
     bool useGraph = true;
+    // Masked apply_reset_state in one fused kernel (CARLB_FUSED_RESET=0: one kernel per part).
+    bool fusedReset = true;
+    // Obs / state rows written through per-warp staging tiles (CARLB_STAGED_PACK=0: a thread per row).
+    bool stagedPack = true;
     int* tickDev = nullptr;
     struct TickGraph { int kind, nTicks; bool diag, timing; cudaGraphExec_t exec; };
     std::vector<TickGraph> graphs;
@@ -140,6 +144,7 @@ struct carlb_env
         g.simOut = simOut;
         g.nSim = cfg.n_sim;
         g.nCars = nCars;
+        g.stagedPack = stagedPack;
         g.nBlue = cfg.n_blue;
         g.nOrange = cfg.n_orange;
         g.seed = cfg.seed;
@@ -450,6 +455,8 @@ static carlb_status initEnv(carlb_env* p, const carlb_config* cfg)
     ECHECK(p, allocZero(p, &p->episodeTicks, (size_t)cfg->n_sim));
     ECHECK(p, allocZero(p, &p->tScoreDiff, (size_t)cfg->n_sim));
     ECHECK(p, allocZero(p, &p->tEpisodeTicks, (size_t)cfg->n_sim));
+    if (const char* fr = std::getenv("CARLB_FUSED_RESET")) p->fusedReset = std::atoi(fr) != 0;
+    if (const char* sp = std::getenv("CARLB_STAGED_PACK")) p->stagedPack = std::atoi(sp) != 0;
     {
         const char* path = std::getenv("CARLB_TICK_PATH");
         p->staged = !(path && std::string(path) == "fused");
@@ -802,7 +809,6 @@ carlb_status carlb_apply_reset_state(carlb_env* e, int32_t n, const float* ballP
 {
     if (!e) return fail(nullptr, CARLB_ERR_VALUE, "env is null");
     if (mask && indices) return fail(e, CARLB_ERR_VALUE, "specify reset_mask or simulation_indices, not both");
-    if (mask && indices) return fail(e, CARLB_ERR_VALUE, "specify reset_mask or simulation_indices, not both");
     if (mask) n = e->cfg.n_sim;
     if (n < 0 || n > e->cfg.n_sim) return fail(e, CARLB_ERR_VALUE, "too many simulation_indices");
     if (!ballPos || !ballVel || !ballAng || !carPos || !carRot || !carVel || !carAng || !demoed)
@@ -811,10 +817,19 @@ carlb_status carlb_apply_reset_state(carlb_env* e, int32_t n, const float* ballP
         return fail(e, CARLB_ERR_VALUE, "blue_score, orange_score and episode_ticks must be supplied together");
     if (n == 0) return CARLB_OK;
     const GView g = e->view();
+    const BallInputs ball{ ballPos, ballVel, ballAng };
+    const CarInputs cars{ carPos, carRot, carVel, carAng, demoed, demoedIsByte, boost, internal };
+    if (mask && e->fusedReset)
+    {
+        const PackTargets pk{ e->obs, e->obsDim, e->cfg.invert_orange, e->cfg.normalize, e->cfg.previous_controls,
+                              e->packed, e->stateDim, e->tick, e->outputs() };
+        launchResetMasked(g, e->arena(), ball, cars, MatchInputs{ blue, orange, ticks }, mask, pk, e->stream);
+        ECHECK(e, cudaGetLastError());
+        return CARLB_OK;
+    }
     launchResetPads(g, n, indices, mask, e->stream);
-    launchSetBall(g, BallInputs{ ballPos, ballVel, ballAng }, n, indices, mask, e->stream);
-    launchSetCar(g, e->arena(), CarInputs{ carPos, carRot, carVel, carAng, demoed, demoedIsByte, boost, internal }, n,
-                 indices, mask, e->stream);
+    launchSetBall(g, ball, n, indices, mask, e->stream);
+    launchSetCar(g, e->arena(), cars, n, indices, mask, e->stream);
     if (blue) launchSetMatch(g, blue, orange, ticks, n, indices, mask, e->stream);
     packCurrent(e, mask);
     ECHECK(e, cudaGetLastError());

@@ -171,72 +171,234 @@ __global__ void resetDonesKernel(GView g, int tick, int maxTicks, int overtimeTi
 
 __device__ __forceinline__ V3 obsVec(V3 v, bool inv) { return inv ? V3{ -v.x, -v.y, v.z } : v; }
 
-__device__ void packCar(const GView& g, long long car, bool inv, float* o, int& k)
+// Output rows (obs, state) are produced by one row function per kind, written
+// through an emitter: put(v) appends v, putN(v, d) appends v / d when the row is
+// normalised (the division the reference applies in place after packing,
+// Observations.cuh normalizeObservations), else v.
+
+// Emitter writing a row straight to memory (one thread per row).
+struct DirectRow
 {
-    const V3 pos = obsVec(g.car.v(C_POS, car), inv);
-    const V3 vel = obsVec(g.car.v(C_VEL, car), inv);
-    const V3 ang = obsVec(g.car.v(C_ANG, car), inv);
+    float* o;
+    int k;
+    bool normalize;
+    __device__ void put(float v) { o[k++] = v; }
+    __device__ void putN(float v, float d) { o[k++] = normalize ? v / d : v; }
+};
+
+// Emitter of a warp that writes 32 rows of rowLen floats lying back to back in
+// memory (row r at out + r * rowLen, lane r produces row r).  Values go to a
+// per-warp tile, 32 columns at a time; a full tile is written as 32 runs of
+// consecutive floats, one row each, so every store of the warp is one coalesced
+// run instead of 32 scattered words.  All 32 lanes must emit the same number of
+// values in the same order; rows whose bit in `rows` is clear are not written.
+struct WarpRows
+{
+    float (*tile)[33];
+    float* out;
+    int rowLen, lane, k;
+    unsigned rows;
+    bool normalize;
+    __device__ void put(float v)
+    {
+        tile[lane][k & 31] = v;
+        if ((++k & 31) == 0) flush(32);
+    }
+    __device__ void putN(float v, float d) { put(normalize ? v / d : v); }
+    __device__ void finish()
+    {
+        if (k & 31) flush(k & 31);
+    }
+    // Out of line: a row emits hundreds of values, and an inlined flush at every
+    // emit would bloat the kernel past the instruction cache.
+    __device__ __noinline__ void flush(int n)
+    {
+        __syncwarp();
+        const int c0 = k - n;
+        if (lane < n)
+        {
+            #pragma unroll 4
+            for (int r = 0; r < 32; r++)
+                if ((rows >> r) & 1u) out[(long long)r * rowLen + c0 + lane] = tile[r][lane];
+        }
+        __syncwarp();
+    }
+};
+
+constexpr float OBS_ARENA_DIAGONAL = 14692.54f;
+
+__device__ __forceinline__ float arenaScale(int a) { return a == 0 ? ARENA_MAX_X : a == 1 ? ARENA_MAX_Y : ARENA_MAX_Z; }
+
+// Every segment of a row loads its words before it emits anything: an emitter
+// may store to global memory, and a load placed after a store it might alias
+// cannot be hoisted, so loads interleaved with emits would each wait a full
+// memory round trip.
+
+// One car block (OBS_PER_CAR values): pose, velocities, axes, boost and flags.
+template <class E>
+__device__ void emitCar(const GView& g, long long car, bool inv, E& e)
+{
+    const V3 rawPos = g.car.v(C_POS, car), rawVel = g.car.v(C_VEL, car), rawAng = g.car.v(C_ANG, car);
     const Q4 rot = g.car.q(C_ROT, car);
+    const float boost = g.car.f(C_INT + I_BOOST, car);
+    const int onGround = g.car.n(C_INT + I_ON_GROUND, car), demoed = g.car.n(C_DEMOED, car);
+    const int flipped = g.car.n(C_INT + I_HAS_FLIPPED, car), doubled = g.car.n(C_INT + I_HAS_DOUBLE_JUMPED, car);
+    const int boosting = g.car.n(C_INT + I_IS_BOOSTING, car);
+    const V3 pos = obsVec(rawPos, inv), vel = obsVec(rawVel, inv), ang = obsVec(rawAng, inv);
     const V3 fwd = obsVec(rotate(rot, axisVec(0)), inv);
     const V3 up = obsVec(rotate(rot, axisVec(2)), inv);
-    o[k++] = pos.x; o[k++] = pos.y; o[k++] = pos.z;
-    o[k++] = vel.x; o[k++] = vel.y; o[k++] = vel.z;
-    o[k++] = ang.x; o[k++] = ang.y; o[k++] = ang.z;
-    o[k++] = fwd.x; o[k++] = fwd.y; o[k++] = fwd.z;
-    o[k++] = up.x; o[k++] = up.y; o[k++] = up.z;
-    o[k++] = g.car.f(C_INT + I_BOOST, car);
-    o[k++] = (float)g.car.n(C_INT + I_ON_GROUND, car);
-    o[k++] = (float)(g.car.n(C_DEMOED, car) != 0);
-    o[k++] = (float)g.car.n(C_INT + I_HAS_FLIPPED, car);
-    o[k++] = (float)g.car.n(C_INT + I_HAS_DOUBLE_JUMPED, car);
-    o[k++] = (float)g.car.n(C_INT + I_IS_BOOSTING, car);
+    e.putN(pos.x, arenaScale(0)); e.putN(pos.y, arenaScale(1)); e.putN(pos.z, arenaScale(2));
+    e.putN(vel.x, CAR_MAX_SPEED); e.putN(vel.y, CAR_MAX_SPEED); e.putN(vel.z, CAR_MAX_SPEED);
+    e.putN(ang.x, CAR_MAX_ANG_SPEED); e.putN(ang.y, CAR_MAX_ANG_SPEED); e.putN(ang.z, CAR_MAX_ANG_SPEED);
+    e.put(fwd.x); e.put(fwd.y); e.put(fwd.z);
+    e.put(up.x); e.put(up.y); e.put(up.z);
+    e.putN(boost, BOOST_MAX);
+    e.put((float)onGround);
+    e.put((float)(demoed != 0));
+    e.put((float)flipped);
+    e.put((float)doubled);
+    e.put((float)boosting);
 }
 
-__device__ void packRelative(const GView& g, long long car, V3 egoPos, V3 egoVel, bool inv, float* o, int& k)
+// The sim's pad cooldowns in emission order (mirrored for an inverted row).
+__device__ __forceinline__ void loadPads(const GView& g, int sim, bool inv, float* cd)
 {
-    const V3 rp = obsVec(g.car.v(C_POS, car) - egoPos, inv);
-    const V3 rv = obsVec(g.car.v(C_VEL, car) - egoVel, inv);
-    o[k++] = rp.x; o[k++] = rp.y; o[k++] = rp.z;
-    o[k++] = rv.x; o[k++] = rv.y; o[k++] = rv.z;
+    #pragma unroll
+    for (int p = 0; p < NUM_BOOST_PADS; p++) cd[p] = g.sim.f(S_PADS + (inv ? c_tables.padMirror[p] : p), sim);
 }
 
-__device__ void normalizeObs(float* o, int nCars)
+// j-th other car of `obs` (0 <= j < nCars - 1): its teammates in car order, then
+// the opponents in car order.
+__device__ __forceinline__ int otherCar(const GView& g, int obs, int j)
 {
-    constexpr float arenaDiagonal = 14692.54f;
-    const float scale[3] = { ARENA_MAX_X, ARENA_MAX_Y, ARENA_MAX_Z };
-    for (int a = 0; a < 3; a++) o[OBS_POS + a] /= scale[a];
-    for (int a = 0; a < 3; a++) o[OBS_VEL + a] /= BALL_MAX_SPEED;
-    for (int a = 0; a < 3; a++) o[OBS_ANG + a] /= BALL_MAX_ANG_SPEED;
-    for (int car = 0; car < nCars; car++)
+    const bool orange = obs >= g.nBlue;
+    const int teamStart = orange ? g.nBlue : 0, teamSize = orange ? g.nCars - g.nBlue : g.nBlue;
+    const int oppStart = orange ? 0 : g.nBlue;
+    if (j < teamSize - 1)
     {
-        const int off = OBS_BALL + car * OBS_PER_CAR;
-        for (int a = 0; a < 3; a++) o[off + OBS_POS + a] /= scale[a];
-        for (int a = 0; a < 3; a++) o[off + OBS_VEL + a] /= CAR_MAX_SPEED;
-        for (int a = 0; a < 3; a++) o[off + OBS_ANG + a] /= CAR_MAX_ANG_SPEED;
-        o[off + OBS_BOOST] /= BOOST_MAX;
+        const int c = teamStart + j;
+        return c >= obs ? c + 1 : c;
     }
-    const int distOff = OBS_BALL + nCars * OBS_PER_CAR + NUM_BOOST_PADS;
-    for (int p = 0; p < NUM_BOOST_PADS; p++) o[distOff + p] /= arenaDiagonal;
-    int rel = distOff + NUM_BOOST_PADS;
-    for (int a = 0; a < 3; a++)
-    {
-        o[rel + a] /= 2.f * scale[a];
-        o[rel + OBS_VECTOR_SIZE + a] /= BALL_MAX_SPEED + CAR_MAX_SPEED;
-    }
-    rel += OBS_RELATIVE_EGO_BALL;
-    for (int car = 1; car < nCars; car++)
-    {
-        for (int a = 0; a < 3; a++)
-        {
-            o[rel + a] /= 2.f * scale[a];
-            o[rel + OBS_VECTOR_SIZE + a] /= 2.f * CAR_MAX_SPEED;
-        }
-        rel += OBS_RELATIVE_PER_OTHER_CAR;
-    }
-    for (int goal = 0; goal < 2; goal++)
-        for (int a = 0; a < 3; a++) o[rel + goal * OBS_VECTOR_SIZE + a] /= 2.f * scale[a];
+    return oppStart + (j - (teamSize - 1));
 }
 
+// Observation row of car `obs` of `sim` (src/EnvIO.cu:47-80, Observations.cuh:97-317).
+template <class E>
+__device__ void emitObsRow(const GView& g, E& e, int invertOrange, int previousControls, int sim, int obs)
+{
+    const long long base = (long long)sim * g.nCars;
+    const bool orange = obs >= g.nBlue;
+    const bool inv = invertOrange && orange;
+    const V3 rawBallPos = g.sim.v(S_BPOS, sim);
+    const V3 rawBallVel = g.sim.v(S_BVEL, sim);
+    const V3 egoPos = g.car.v(C_POS, base + obs);
+    const V3 egoVel = g.car.v(C_VEL, base + obs);
+    const V3 bp = obsVec(rawBallPos, inv), bv = obsVec(rawBallVel, inv), ba = obsVec(g.sim.v(S_BANG, sim), inv);
+    e.putN(bp.x, arenaScale(0)); e.putN(bp.y, arenaScale(1)); e.putN(bp.z, arenaScale(2));
+    e.putN(bv.x, BALL_MAX_SPEED); e.putN(bv.y, BALL_MAX_SPEED); e.putN(bv.z, BALL_MAX_SPEED);
+    e.putN(ba.x, BALL_MAX_ANG_SPEED); e.putN(ba.y, BALL_MAX_ANG_SPEED); e.putN(ba.z, BALL_MAX_ANG_SPEED);
+    emitCar(g, base + obs, inv, e);
+    for (int j = 0; j < g.nCars - 1; j++) emitCar(g, base + otherCar(g, obs, j), inv, e);
+
+    float cd[NUM_BOOST_PADS];
+    loadPads(g, sim, inv, cd);
+    #pragma unroll
+    for (int p = 0; p < NUM_BOOST_PADS; p++) e.put(cd[p] <= 0.f);
+    for (int p = 0; p < NUM_BOOST_PADS; p++)
+    {
+        const int pad = inv ? c_tables.padMirror[p] : p;
+        e.putN(len(egoPos - V3{ c_tables.padX[pad], c_tables.padY[pad], c_tables.padZ[pad] }), OBS_ARENA_DIAGONAL);
+    }
+    const V3 eb = obsVec(rawBallPos - egoPos, inv), ebv = obsVec(rawBallVel - egoVel, inv);
+    e.putN(eb.x, 2.f * arenaScale(0)); e.putN(eb.y, 2.f * arenaScale(1)); e.putN(eb.z, 2.f * arenaScale(2));
+    e.putN(ebv.x, BALL_MAX_SPEED + CAR_MAX_SPEED); e.putN(ebv.y, BALL_MAX_SPEED + CAR_MAX_SPEED);
+    e.putN(ebv.z, BALL_MAX_SPEED + CAR_MAX_SPEED);
+    for (int j = 0; j < g.nCars - 1; j++)
+    {
+        const long long car = base + otherCar(g, obs, j);
+        const V3 op = g.car.v(C_POS, car), ov = g.car.v(C_VEL, car);
+        const V3 rp = obsVec(op - egoPos, inv);
+        const V3 rv = obsVec(ov - egoVel, inv);
+        e.putN(rp.x, 2.f * arenaScale(0)); e.putN(rp.y, 2.f * arenaScale(1)); e.putN(rp.z, 2.f * arenaScale(2));
+        e.putN(rv.x, 2.f * CAR_MAX_SPEED); e.putN(rv.y, 2.f * CAR_MAX_SPEED); e.putN(rv.z, 2.f * CAR_MAX_SPEED);
+    }
+
+    const long long ego = base + obs;
+    const bool hasFlipped = g.car.n(C_INT + I_HAS_FLIPPED, ego) != 0;
+    const bool hasDouble = g.car.n(C_INT + I_HAS_DOUBLE_JUMPED, ego) != 0;
+    const float airSinceJump = g.car.f(C_INT + I_AIR_TIME_SINCE_JUMP, ego);
+    const int hasJumped = g.car.n(C_INT + I_HAS_JUMPED, ego), isJumping = g.car.n(C_INT + I_IS_JUMPING, ego);
+    const int isFlipping = g.car.n(C_INT + I_IS_FLIPPING, ego);
+    const float flipTime = g.car.f(C_INT + I_FLIP_TIME, ego), demoTimer = g.car.f(C_DEMO_TIMER, ego);
+    float prev[8];
+    if (previousControls)
+    {
+        #pragma unroll
+        for (int c = 0; c < 5; c++) prev[c] = g.out.f(O_CONTROLS + c, ego);
+        #pragma unroll
+        for (int c = 5; c < 8; c++) prev[c] = (float)g.out.n(O_CONTROLS + c, ego);
+    }
+
+    const float ownGoalY = orange ? SOCCAR_GOAL_CENTER_Y : -SOCCAR_GOAL_CENTER_Y;
+    const V3 ownGoal = { 0.f, ownGoalY, SOCCAR_GOAL_CENTER_Z };
+    const V3 oppGoal = { 0.f, -ownGoalY, SOCCAR_GOAL_CENTER_Z };
+    const V3 bo = obsVec(ownGoal - rawBallPos, inv), bq = obsVec(oppGoal - rawBallPos, inv);
+    e.putN(bo.x, 2.f * arenaScale(0)); e.putN(bo.y, 2.f * arenaScale(1)); e.putN(bo.z, 2.f * arenaScale(2));
+    e.putN(bq.x, 2.f * arenaScale(0)); e.putN(bq.y, 2.f * arenaScale(1)); e.putN(bq.z, 2.f * arenaScale(2));
+
+    const bool flipAvailable = !hasFlipped && !hasDouble && airSinceJump < DOUBLEJUMP_MAX_DELAY;
+    e.put((float)flipAvailable);
+    e.put(flipAvailable ? fmaxf(0.f, DOUBLEJUMP_MAX_DELAY - airSinceJump) : 0.f);
+    e.put((float)hasJumped);
+    e.put((float)isJumping);
+    e.put((float)isFlipping);
+    e.put(flipTime);
+    e.put(demoTimer);
+    if (previousControls)
+    {
+        #pragma unroll
+        for (int c = 0; c < 8; c++) e.put(prev[c]);
+    }
+}
+
+// Canonical state row of `sim` (Observations.cuh:320-356): ball, each car's
+// block and ball-touch flag (a touch within `touchWindow` ticks), pad states.
+template <class E>
+__device__ void emitStateRow(const GView& g, E& e, int tick, int touchWindow, int sim)
+{
+    const V3 bp = g.sim.v(S_BPOS, sim), bv = g.sim.v(S_BVEL, sim), ba = g.sim.v(S_BANG, sim);
+    e.put(bp.x); e.put(bp.y); e.put(bp.z);
+    e.put(bv.x); e.put(bv.y); e.put(bv.z);
+    e.put(ba.x); e.put(ba.y); e.put(ba.z);
+    for (int c = 0; c < g.nCars; c++)
+    {
+        const long long car = (long long)sim * g.nCars + c;
+        const int touchTick = g.car.n(C_BALL_CONTACT_TICK, car);
+        emitCar(g, car, false, e);
+        e.put(touchTick > tick - touchWindow);
+    }
+    float cd[NUM_BOOST_PADS];
+    loadPads(g, sim, false, cd);
+    #pragma unroll
+    for (int p = 0; p < NUM_BOOST_PADS; p++) e.put(cd[p] <= 0.f);
+}
+
+__device__ void packObsAgent(const GView& g, float* out, int obsDim, int invertOrange, int normalize,
+                             int previousControls, int sim, int obs)
+{
+    DirectRow e{ out + ((long long)sim * g.nCars + obs) * obsDim, 0, normalize != 0 };
+    emitObsRow(g, e, invertOrange, previousControls, sim, obs);
+}
+
+__device__ void packStateSim(const GView& g, float* out, int stateDim, int tick, int touchWindow, int sim)
+{
+    DirectRow e{ out + (long long)sim * stateDim, 0, false };
+    emitStateRow(g, e, tick, touchWindow, sim);
+}
+
+constexpr int PACK_THREADS = 128;
+
+// One thread per row, written directly.
 __global__ void packObsKernel(GView g, float* out, const uint8_t* mask, int obsDim, int invertOrange,
                               int normalize, int previousControls)
 {
@@ -244,90 +406,49 @@ __global__ void packObsKernel(GView g, float* out, const uint8_t* mask, int obsD
     if (agent >= (long long)g.nSim * g.nCars) return;
     const int sim = (int)(agent / g.nCars);
     if (mask && !mask[sim]) return;
-    const int obs = (int)(agent - (long long)sim * g.nCars);
-    const long long base = (long long)sim * g.nCars;
-    const bool orange = obs >= g.nBlue;
-    const bool inv = invertOrange && orange;
-    float* o = out + agent * obsDim;
-    int k = 0;
-
-    const V3 rawBallPos = g.sim.v(S_BPOS, sim);
-    const V3 rawBallVel = g.sim.v(S_BVEL, sim);
-    const V3 egoPos = g.car.v(C_POS, base + obs);
-    const V3 egoVel = g.car.v(C_VEL, base + obs);
-    const V3 bp = obsVec(rawBallPos, inv), bv = obsVec(rawBallVel, inv), ba = obsVec(g.sim.v(S_BANG, sim), inv);
-    o[k++] = bp.x; o[k++] = bp.y; o[k++] = bp.z;
-    o[k++] = bv.x; o[k++] = bv.y; o[k++] = bv.z;
-    o[k++] = ba.x; o[k++] = ba.y; o[k++] = ba.z;
-    packCar(g, base + obs, inv, o, k);
-
-    const int teamStart = orange ? g.nBlue : 0, teamEnd = orange ? g.nCars : g.nBlue;
-    const int oppStart = orange ? 0 : g.nBlue, oppEnd = orange ? g.nBlue : g.nCars;
-    for (int c = teamStart; c < teamEnd; c++)
-        if (c != obs) packCar(g, base + c, inv, o, k);
-    for (int c = oppStart; c < oppEnd; c++) packCar(g, base + c, inv, o, k);
-
-    for (int p = 0; p < NUM_BOOST_PADS; p++)
-    {
-        const int pad = inv ? c_tables.padMirror[p] : p;
-        o[k++] = g.sim.f(S_PADS + pad, sim) <= 0.f;
-    }
-    for (int p = 0; p < NUM_BOOST_PADS; p++)
-    {
-        const int pad = inv ? c_tables.padMirror[p] : p;
-        o[k++] = len(egoPos - V3{ c_tables.padX[pad], c_tables.padY[pad], c_tables.padZ[pad] });
-    }
-    const V3 eb = obsVec(rawBallPos - egoPos, inv), ebv = obsVec(rawBallVel - egoVel, inv);
-    o[k++] = eb.x; o[k++] = eb.y; o[k++] = eb.z;
-    o[k++] = ebv.x; o[k++] = ebv.y; o[k++] = ebv.z;
-    for (int c = teamStart; c < teamEnd; c++)
-        if (c != obs) packRelative(g, base + c, egoPos, egoVel, inv, o, k);
-    for (int c = oppStart; c < oppEnd; c++) packRelative(g, base + c, egoPos, egoVel, inv, o, k);
-
-    const float ownGoalY = orange ? SOCCAR_GOAL_CENTER_Y : -SOCCAR_GOAL_CENTER_Y;
-    const V3 ownGoal = { 0.f, ownGoalY, SOCCAR_GOAL_CENTER_Z };
-    const V3 oppGoal = { 0.f, -ownGoalY, SOCCAR_GOAL_CENTER_Z };
-    const V3 bo = obsVec(ownGoal - rawBallPos, inv), bq = obsVec(oppGoal - rawBallPos, inv);
-    o[k++] = bo.x; o[k++] = bo.y; o[k++] = bo.z;
-    o[k++] = bq.x; o[k++] = bq.y; o[k++] = bq.z;
-
-    const long long ego = base + obs;
-    const bool hasFlipped = g.car.n(C_INT + I_HAS_FLIPPED, ego) != 0;
-    const bool hasDouble = g.car.n(C_INT + I_HAS_DOUBLE_JUMPED, ego) != 0;
-    const float airSinceJump = g.car.f(C_INT + I_AIR_TIME_SINCE_JUMP, ego);
-    const bool flipAvailable = !hasFlipped && !hasDouble && airSinceJump < DOUBLEJUMP_MAX_DELAY;
-    o[k++] = (float)flipAvailable;
-    o[k++] = flipAvailable ? fmaxf(0.f, DOUBLEJUMP_MAX_DELAY - airSinceJump) : 0.f;
-    o[k++] = (float)g.car.n(C_INT + I_HAS_JUMPED, ego);
-    o[k++] = (float)g.car.n(C_INT + I_IS_JUMPING, ego);
-    o[k++] = (float)g.car.n(C_INT + I_IS_FLIPPING, ego);
-    o[k++] = g.car.f(C_INT + I_FLIP_TIME, ego);
-    o[k++] = g.car.f(C_DEMO_TIMER, ego);
-    if (previousControls)
-    {
-        for (int c = 0; c < 5; c++) o[k++] = g.out.f(O_CONTROLS + c, ego);
-        for (int c = 5; c < 8; c++) o[k++] = (float)g.out.n(O_CONTROLS + c, ego);
-    }
-    if (normalize) normalizeObs(o, g.nCars);
+    packObsAgent(g, out, obsDim, invertOrange, normalize, previousControls, sim, (int)(agent - (long long)sim * g.nCars));
 }
 
 __global__ void packStateKernel(GView g, float* out, int stateDim, int tick, int touchWindow, const uint8_t* mask)
 {
     const int sim = blockIdx.x * blockDim.x + threadIdx.x;
     if (sim >= g.nSim || (mask && !mask[sim])) return;
-    float* o = out + (long long)sim * stateDim;
-    int k = 0;
-    const V3 bp = g.sim.v(S_BPOS, sim), bv = g.sim.v(S_BVEL, sim), ba = g.sim.v(S_BANG, sim);
-    o[k++] = bp.x; o[k++] = bp.y; o[k++] = bp.z;
-    o[k++] = bv.x; o[k++] = bv.y; o[k++] = bv.z;
-    o[k++] = ba.x; o[k++] = ba.y; o[k++] = ba.z;
-    for (int c = 0; c < g.nCars; c++)
-    {
-        const long long car = (long long)sim * g.nCars + c;
-        packCar(g, car, false, o, k);
-        o[k++] = g.car.n(C_BALL_CONTACT_TICK, car) > tick - touchWindow;
-    }
-    for (int p = 0; p < NUM_BOOST_PADS; p++) o[k++] = g.sim.f(S_PADS + p, sim) <= 0.f;
+    packStateSim(g, out, stateDim, tick, touchWindow, sim);
+}
+
+// A warp per 32 consecutive rows, written through the warp's staging tile.
+// Lanes past the end or outside the mask produce a clamped row that is not
+// written; a warp with no row to write returns at once.
+__global__ void __launch_bounds__(PACK_THREADS, 6) packObsWarpKernel(GView g, float* out, const uint8_t* mask, int obsDim,
+                                                                  int invertOrange, int normalize, int previousControls)
+{
+    __shared__ float tile[PACK_THREADS / 32][32][33];
+    const long long n = (long long)g.nSim * g.nCars;
+    const long long agent = blockIdx.x * (long long)PACK_THREADS + threadIdx.x;
+    const long long a = agent < n ? agent : n - 1;
+    const int sim = (int)(a / g.nCars);
+    const bool write = agent < n && (!mask || mask[sim]);
+    const unsigned rows = __ballot_sync(0xffffffffu, write);
+    if (!rows) return;
+    const int lane = threadIdx.x & 31;
+    WarpRows e{ tile[threadIdx.x >> 5], out + (agent - lane) * obsDim, obsDim, lane, 0, rows, normalize != 0 };
+    emitObsRow(g, e, invertOrange, previousControls, sim, (int)(a - (long long)sim * g.nCars));
+    e.finish();
+}
+
+__global__ void __launch_bounds__(PACK_THREADS) packStateWarpKernel(GView g, float* out, int stateDim, int tick,
+                                                                    int touchWindow, const uint8_t* mask)
+{
+    __shared__ float tile[PACK_THREADS / 32][32][33];
+    const int s = blockIdx.x * PACK_THREADS + threadIdx.x;
+    const int sim = s < g.nSim ? s : g.nSim - 1;
+    const bool write = s < g.nSim && (!mask || mask[sim]);
+    const unsigned rows = __ballot_sync(0xffffffffu, write);
+    if (!rows) return;
+    const int lane = threadIdx.x & 31;
+    WarpRows e{ tile[threadIdx.x >> 5], out + (long long)(s - lane) * stateDim, stateDim, lane, 0, rows, false };
+    emitStateRow(g, e, tick, touchWindow, sim);
+    e.finish();
 }
 
 __global__ void packRewardsDonesKernel(GView g, Outputs out, int tick, int maxTicks, int overtimeTicks, int noTouchTicks)
@@ -350,13 +471,18 @@ __global__ void packRewardsDonesKernel(GView g, Outputs out, int tick, int maxTi
     out.transitionOvertime[sim] = overtime ? 1 : 0;
 }
 
+__device__ void packRawMatchSim(const GView& g, const Outputs& out, int sim)
+{
+    out.scoreDiff[sim] = g.sim.n(S_GOALS + G_BLUE, sim) - g.sim.n(S_GOALS + G_ORANGE, sim);
+    out.episodeTicks[sim] = g.sim.n(S_EP_TICKS, sim);
+    out.overtime[sim] = g.sim.n(S_GOALS + G_OVERTIME, sim) != 0 ? 1 : 0;
+}
+
 __global__ void packRawMatchKernel(GView g, Outputs out, const uint8_t* mask)
 {
     const int sim = blockIdx.x * blockDim.x + threadIdx.x;
     if (sim >= g.nSim || (mask && !mask[sim])) return;
-    out.scoreDiff[sim] = g.sim.n(S_GOALS + G_BLUE, sim) - g.sim.n(S_GOALS + G_ORANGE, sim);
-    out.episodeTicks[sim] = g.sim.n(S_EP_TICKS, sim);
-    out.overtime[sim] = g.sim.n(S_GOALS + G_OVERTIME, sim) != 0 ? 1 : 0;
+    packRawMatchSim(g, out, sim);
 }
 
 // ---- state injection --------------------------------------------------------------------------------
@@ -371,25 +497,26 @@ __device__ __forceinline__ bool selectTarget(const GView& g, int source, const i
     return true;
 }
 
-__global__ void setBallKernel(GView g, BallInputs in, int nSelected, const int64_t* indices, const uint8_t* mask)
+// Input row `src` written to `sim` (src/EnvIO.cu:137-318,603-680).
+__device__ void setBallSim(const GView& g, const BallInputs& in, int src, int sim)
 {
-    const int src = blockIdx.x * blockDim.x + threadIdx.x;
-    int sim;
-    if (src >= nSelected || !selectTarget(g, src, indices, mask, sim)) return;
     g.sim.setv(S_BPOS, sim, V3{ in.pos[3 * src], in.pos[3 * src + 1], in.pos[3 * src + 2] });
     g.sim.setv(S_BVEL, sim, V3{ in.vel[3 * src], in.vel[3 * src + 1], in.vel[3 * src + 2] });
     g.sim.setv(S_BANG, sim, V3{ in.ang[3 * src], in.ang[3 * src + 1], in.ang[3 * src + 2] });
     g.sim.setv(S_BIMP, sim, v3zero());
 }
 
-__global__ void setCarKernel(GView g, CarInputs in, int nSelected, const int64_t* indices, const uint8_t* mask)
+__global__ void setBallKernel(GView g, BallInputs in, int nSelected, const int64_t* indices, const uint8_t* mask)
 {
     const int src = blockIdx.x * blockDim.x + threadIdx.x;
-    if (src >= nSelected * g.nCars) return;
-    const int srcSim = src / g.nCars;
     int sim;
-    if (!selectTarget(g, srcSim, indices, mask, sim)) return;
-    const int local = src - srcSim * g.nCars;
+    if (src >= nSelected || !selectTarget(g, src, indices, mask, sim)) return;
+    setBallSim(g, in, src, sim);
+}
+
+// Input row `src` (= input sim × nCars + local) written to car `local` of `sim`.
+__device__ void setCarOne(const GView& g, const CarInputs& in, int src, int sim, int local)
+{
     const long long car = (long long)sim * g.nCars + local;
     const GlobSoa& c = g.car;
     const float previousBoost = c.f(C_INT + I_BOOST, car);
@@ -459,45 +586,74 @@ __global__ void setCarKernel(GView g, CarInputs in, int nSelected, const int64_t
     }
 }
 
-// Serial suspension raycast of one car against its grid cell, the other cars
-// and the ball (the tick kernel's flattened version gives the same hits).
-__device__ void raycastCar(const GView& g, const ArenaDev& a, long long car, int sim, float* dist, V3* normal, int* src)
+__global__ void setCarKernel(GView g, CarInputs in, int nSelected, const int64_t* indices, const uint8_t* mask)
+{
+    const int src = blockIdx.x * blockDim.x + threadIdx.x;
+    if (src >= nSelected * g.nCars) return;
+    const int srcSim = src / g.nCars;
+    int sim;
+    if (!selectTarget(g, srcSim, indices, mask, sim)) return;
+    setCarOne(g, in, src, sim, src - srcSim * g.nCars);
+}
+
+// Wheel ray set-up of one car: ray starts, direction (-up), the car's up axis
+// and its broadphase cell.
+struct CarRays
+{
+    V3 start[NUM_WHEELS];
+    V3 dir, up;
+    int cell;
+};
+
+__device__ CarRays carRays(const GView& g, long long car)
 {
     const GlobSoa& c = g.car;
     const V3 pos = c.v(C_POS, car), vel = c.v(C_VEL, car), ang = c.v(C_ANG, car), cen = c.v(C_CEN, car);
     const Q4 rot = c.q(C_ROT, car);
-    const V3 up = rotate(rot, axisVec(2));
-    const V3 dir = neg(up);
-    V3 start[NUM_WHEELS];
-    for (int w = 0; w < NUM_WHEELS; w++)
-    {
-        start[w] = cen + rotate(rot, suspConnection(w));
-        dist[w] = suspRayLength(w) + 1.f;
-        normal[w] = up;
-        src[w] = WHEEL_NONE;
-    }
-    const int cell = broadphaseCell(pos, vel, ang, cen, rot);
-    for (int e = a.cellStart[cell]; e < a.cellStart[cell + 1]; e++)
+    CarRays r;
+    r.up = rotate(rot, axisVec(2));
+    r.dir = neg(r.up);
+    for (int w = 0; w < NUM_WHEELS; w++) r.start[w] = cen + rotate(rot, suspConnection(w));
+    r.cell = broadphaseCell(pos, vel, ang, cen, rot);
+    return r;
+}
+
+// Möller–Trumbore hit distance of a wheel ray against a triangle given by v0
+// and its edges (pv = dir × e2, invDet = 1 / (e1 · pv)); false when missed or
+// not closer than `limit`.
+__device__ __forceinline__ bool wheelTriHit(V3 start, V3 dir, V3 v0, V3 e1, V3 e2, V3 pv, float invDet, float limit,
+                                            float& d)
+{
+    const V3 tv = start - v0;
+    const float u = invDet * dot(tv, pv);
+    if (u < 0.f || u > 1.f) return false;
+    const V3 qv = cross(tv, e1);
+    const float v = invDet * dot(dir, qv);
+    if (v < 0.f || u + v > 1.f) return false;
+    d = invDet * dot(e2, qv);
+    return !(d <= 0.f || d >= limit);
+}
+
+// Serial arena pass of the wheel rays over the cell's triangles in candidate
+// order (a strictly closer hit replaces the previous one; a degenerate winning
+// triangle keeps the previous normal).  Wheels outside [w0, w1) are untouched.
+__device__ void arenaRaysSerial(const ArenaDev& a, const CarRays& r, int w0, int w1, float* dist, V3* normal, int* src)
+{
+    for (int e = a.cellStart[r.cell]; e < a.cellStart[r.cell + 1]; e++)
     {
         const int tri = a.cellTris[e];
         const float4 p0 = a.triV[3 * tri], p1 = a.triV[3 * tri + 1], p2 = a.triV[3 * tri + 2];
         const V3 v0 = { p0.x, p0.y, p0.z };
         const V3 e1 = V3{ p1.x, p1.y, p1.z } - v0;
         const V3 e2 = V3{ p2.x, p2.y, p2.z } - v0;
-        const V3 pv = cross(dir, e2);
+        const V3 pv = cross(r.dir, e2);
         const float det = dot(e1, pv);
         if (fabsf(det) < RAY_PARALLEL_EPS) continue;
         const float invDet = 1.f / det;
-        for (int w = 0; w < NUM_WHEELS; w++)
+        for (int w = w0; w < w1; w++)
         {
-            const V3 tv = start[w] - v0;
-            const float u = invDet * dot(tv, pv);
-            if (u < 0.f || u > 1.f) continue;
-            const V3 qv = cross(tv, e1);
-            const float v = invDet * dot(dir, qv);
-            if (v < 0.f || u + v > 1.f) continue;
-            const float d = invDet * dot(e2, qv);
-            if (d <= 0.f || d >= dist[w]) continue;
+            float d;
+            if (!wheelTriHit(r.start[w], r.dir, v0, e1, e2, pv, invDet, dist[w], d)) continue;
             dist[w] = d;
             src[w] = WHEEL_ARENA;
             V3 n = cross(e1, e2);
@@ -505,11 +661,30 @@ __device__ void raycastCar(const GView& g, const ArenaDev& a, long long car, int
             if (nl > 1e-12f)
             {
                 n = n * rsqrtf(nl);
-                if (dot(n, dir) > 0.f) n = neg(n);
+                if (dot(n, r.dir) > 0.f) n = neg(n);
                 normal[w] = n;
             }
         }
     }
+}
+
+__device__ void initWheelRays(const CarRays& r, float* dist, V3* normal, int* src)
+{
+    for (int w = 0; w < NUM_WHEELS; w++)
+    {
+        dist[w] = suspRayLength(w) + 1.f;
+        normal[w] = r.up;
+        src[w] = WHEEL_NONE;
+    }
+}
+
+// The wheel rays against the sim's other cars (in car order) and the ball,
+// after the arena pass.
+__device__ void carBallRays(const GView& g, long long car, int sim, const CarRays& r, float* dist, V3* normal, int* src)
+{
+    const GlobSoa& c = g.car;
+    const V3* start = r.start;
+    const V3 dir = r.dir;
     const long long base = (long long)sim * g.nCars;
     for (int k = 0; k < g.nCars; k++)
     {
@@ -567,31 +742,20 @@ __device__ void raycastCar(const GView& g, const ArenaDev& a, long long car, int
     }
 }
 
-__global__ void refreshContactsKernel(GView g, ArenaDev a, int nSelected, const int64_t* indices, const uint8_t* mask)
+// Serial suspension raycast of one car against its grid cell, the other cars
+// and the ball (the tick kernel's flattened version gives the same hits).
+__device__ void raycastCar(const GView& g, const ArenaDev& a, long long car, int sim, float* dist, V3* normal, int* src)
 {
-    const int src = blockIdx.x * blockDim.x + threadIdx.x;
-    if (src >= nSelected * g.nCars) return;
-    const int srcSim = src / g.nCars;
-    int sim;
-    if (!selectTarget(g, srcSim, indices, mask, sim)) return;
-    const long long car = (long long)sim * g.nCars + (src - srcSim * g.nCars);
-    float dist[NUM_WHEELS];
-    V3 normal[NUM_WHEELS];
-    int source[NUM_WHEELS];
-    const bool demoed = g.car.n(C_DEMOED, car) != 0;
-    if (demoed)
-    {
-        for (int w = 0; w < NUM_WHEELS; w++)
-        {
-            dist[w] = suspRayLength(w) + 1.f;
-            normal[w] = axisVec(2);
-            source[w] = WHEEL_NONE;
-        }
-    }
-    else
-    {
-        raycastCar(g, a, car, sim, dist, normal, source);
-    }
+    const CarRays r = carRays(g, car);
+    initWheelRays(r, dist, normal, src);
+    arenaRaysSerial(a, r, 0, NUM_WHEELS, dist, normal, src);
+    carBallRays(g, car, sim, r, dist, normal, src);
+}
+
+// Stores the wheel ray results and the on-ground flag of a restored car.
+__device__ void storeRefresh(const GView& g, long long car, bool demoed, const float* dist, const V3* normal,
+                             const int* source)
+{
     int contacts = 0;
     for (int w = 0; w < NUM_WHEELS; w++)
     {
@@ -605,12 +769,42 @@ __global__ void refreshContactsKernel(GView g, ArenaDev a, int nSelected, const 
     g.car.n(C_INT + I_ON_GROUND, car) = demoed ? 0 : contacts >= 3;
 }
 
-__global__ void setMatchKernel(GView g, const int32_t* blue, const int32_t* orange, const int32_t* ticks, int nSelected,
-                               const int64_t* indices, const uint8_t* mask)
+__device__ void demoedWheelRays(float* dist, V3* normal, int* source)
+{
+    for (int w = 0; w < NUM_WHEELS; w++)
+    {
+        dist[w] = suspRayLength(w) + 1.f;
+        normal[w] = axisVec(2);
+        source[w] = WHEEL_NONE;
+    }
+}
+
+// Wheel contacts and on-ground flag of a restored car (refreshRestoredCarContacts).
+__device__ void refreshCarOne(const GView& g, const ArenaDev& a, int sim, int local)
+{
+    const long long car = (long long)sim * g.nCars + local;
+    float dist[NUM_WHEELS];
+    V3 normal[NUM_WHEELS];
+    int source[NUM_WHEELS];
+    const bool demoed = g.car.n(C_DEMOED, car) != 0;
+    if (demoed) demoedWheelRays(dist, normal, source);
+    else raycastCar(g, a, car, sim, dist, normal, source);
+    storeRefresh(g, car, demoed, dist, normal, source);
+}
+
+__global__ void refreshContactsKernel(GView g, ArenaDev a, int nSelected, const int64_t* indices, const uint8_t* mask)
 {
     const int src = blockIdx.x * blockDim.x + threadIdx.x;
+    if (src >= nSelected * g.nCars) return;
+    const int srcSim = src / g.nCars;
     int sim;
-    if (src >= nSelected || !selectTarget(g, src, indices, mask, sim)) return;
+    if (!selectTarget(g, srcSim, indices, mask, sim)) return;
+    refreshCarOne(g, a, sim, src - srcSim * g.nCars);
+}
+
+__device__ void setMatchSim(const GView& g, const int32_t* blue, const int32_t* orange, const int32_t* ticks, int src,
+                            int sim)
+{
     g.sim.n(S_GOALS + G_BLUE, sim) = blue[src];
     g.sim.n(S_GOALS + G_ORANGE, sim) = orange[src];
     g.sim.n(S_GOALS + G_LAST_SCORER, sim) = 0;
@@ -618,12 +812,262 @@ __global__ void setMatchKernel(GView g, const int32_t* blue, const int32_t* oran
     g.sim.n(S_EP_TICKS, sim) = ticks[src];
 }
 
+__global__ void setMatchKernel(GView g, const int32_t* blue, const int32_t* orange, const int32_t* ticks, int nSelected,
+                               const int64_t* indices, const uint8_t* mask)
+{
+    const int src = blockIdx.x * blockDim.x + threadIdx.x;
+    int sim;
+    if (src >= nSelected || !selectTarget(g, src, indices, mask, sim)) return;
+    setMatchSim(g, blue, orange, ticks, src, sim);
+}
+
+__device__ void resetPadsSim(const GView& g, int sim)
+{
+    for (int p = 0; p < NUM_BOOST_PADS; p++) g.sim.f(S_PADS + p, sim) = 0.f;
+}
+
 __global__ void resetPadsKernel(GView g, int nSelected, const int64_t* indices, const uint8_t* mask)
 {
     const int src = blockIdx.x * blockDim.x + threadIdx.x;
     int sim;
     if (src >= nSelected || !selectTarget(g, src, indices, mask, sim)) return;
-    for (int p = 0; p < NUM_BOOST_PADS; p++) g.sim.f(S_PADS + p, sim) = 0.f;
+    resetPadsSim(g, sim);
+}
+
+// Emitter of a warp that writes 32 rows of rowLen floats at per-lane row
+// addresses (lane r's row at `row`), through the same per-warp tile as WarpRows:
+// each store of the warp is a run of consecutive floats of one row.  All lanes
+// emit the same sequence; rows whose bit in `rows` is clear are not written.
+struct WarpRowsAt
+{
+    float (*tile)[33];
+    float* row;
+    int lane, k;
+    unsigned rows;
+    bool normalize;
+    __device__ void put(float v)
+    {
+        tile[lane][k & 31] = v;
+        if ((++k & 31) == 0) flush(32);
+    }
+    __device__ void putN(float v, float d) { put(normalize ? v / d : v); }
+    __device__ void finish()
+    {
+        if (k & 31) flush(k & 31);
+    }
+    // Out of line: a row emits hundreds of values, and an inlined flush at every
+    // emit would bloat the kernel past the instruction cache.
+    __device__ __noinline__ void flush(int n)
+    {
+        __syncwarp();
+        const int c0 = k - n;
+        for (int r = 0; r < 32; r++)
+        {
+            float* dst = reinterpret_cast<float*>(__shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(row), r));
+            if (((rows >> r) & 1u) && lane < n) dst[c0 + lane] = tile[r][lane];
+        }
+        __syncwarp();
+    }
+};
+
+// Masked apply_reset_state in one launch (python/carl.cu:508-666 with reset_mask:
+// pads, ball, cars, contact refresh, match state, then obs / state / raw match
+// outputs of the masked sims).  Each CTA owns a chunk of RESET_CHUNK sims: it
+// lists the chunk's selected sims (ascending), then steps them in rounds of
+// whole sims, one thread per car, so the refresh (which casts against the sim's
+// other cars and ball) and the packing (which reads the whole sim) follow the
+// writes after a CTA barrier.  With few selected sims every CTA is resident in
+// one wave and does one short round.  Each phase runs the same per-item code as
+// the separate kernels.
+constexpr int RESET_THREADS = 128;
+constexpr int RESET_CHUNK = 512;  // sims per CTA (a multiple of RESET_THREADS)
+
+__device__ __forceinline__ unsigned long long wheelKey(float dist, unsigned cand)
+{
+    return ((unsigned long long)__float_as_uint(dist) << 32) | cand;
+}
+
+__global__ void __launch_bounds__(RESET_THREADS) resetMaskedKernel(GView g, ArenaDev a, BallInputs ball, CarInputs cars,
+                                                                  MatchInputs match, const uint8_t* mask, PackTargets pk)
+{
+    __shared__ int selS[RESET_CHUNK];
+    __shared__ int warpCountS[RESET_THREADS / 32];
+    __shared__ unsigned long long keyS[NUM_WHEELS][RESET_THREADS];
+    __shared__ float startS[15][RESET_THREADS];  // wheel ray starts (12), direction (3)
+    __shared__ int firstS[RESET_THREADS], endS[RESET_THREADS], warpSumS[RESET_THREADS / 32];
+    __shared__ float obsTile[RESET_THREADS / 32][32][33];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+    // The chunk's selected sims in ascending order.
+    int nSel = 0;
+    for (int part = 0; part < RESET_CHUNK / RESET_THREADS; part++)
+    {
+        const long long s = (long long)blockIdx.x * RESET_CHUNK + part * RESET_THREADS + tid;
+        const bool pick = s < g.nSim && mask[s] != 0;
+        const unsigned bits = __ballot_sync(0xffffffffu, pick);
+        if (lane == 0) warpCountS[warp] = __popc(bits);
+        __syncthreads();
+        int before = nSel;
+        for (int w = 0; w < warp; w++) before += warpCountS[w];
+        if (pick) selS[before + __popc(bits & ((1u << lane) - 1u))] = (int)s;
+        for (int w = 0; w < RESET_THREADS / 32; w++) nSel += warpCountS[w];
+        __syncthreads();
+    }
+    if (nSel == 0) return;
+
+    const int perRound = RESET_THREADS / g.nCars;
+    const int slot = tid / g.nCars;
+    const int local = tid - slot * g.nCars;
+    for (int round = 0; round < nSel; round += perRound)
+    {
+        const bool on = slot < perRound && round + slot < nSel;
+        const int sim = selS[on ? round + slot : round];  // threads with no car read a valid sim
+        if (on)
+        {
+            if (local == 0)
+            {
+                resetPadsSim(g, sim);
+                setBallSim(g, ball, sim, sim);
+            }
+            setCarOne(g, cars, sim * g.nCars + local, sim, local);
+            if (local == 0 && match.blue) setMatchSim(g, match.blue, match.orange, match.ticks, sim, sim);
+        }
+        __syncthreads();
+        // Contact refresh.  The arena pass of the wheel rays is flattened over the
+        // CTA: every (car, cell triangle) item of the CTA's restored cars is one unit
+        // of work, and a wheel's winner is the least (distance bits, candidate) key,
+        // which is the serial pass's first strictly closest hit.
+        const long long car = (long long)sim * g.nCars + local;
+        const bool demoed = on && g.car.n(C_DEMOED, car) != 0;
+        const bool cast = on && !demoed;
+        CarRays r;
+        if (cast)
+        {
+            r = carRays(g, car);
+            for (int w = 0; w < NUM_WHEELS; w++)
+            {
+                keyS[w][threadIdx.x] = wheelKey(suspRayLength(w) + 1.f, 0xffffffffu);
+                startS[3 * w][threadIdx.x] = r.start[w].x;
+                startS[3 * w + 1][threadIdx.x] = r.start[w].y;
+                startS[3 * w + 2][threadIdx.x] = r.start[w].z;
+            }
+            startS[12][threadIdx.x] = r.dir.x;
+            startS[13][threadIdx.x] = r.dir.y;
+            startS[14][threadIdx.x] = r.dir.z;
+            firstS[threadIdx.x] = a.cellStart[r.cell];
+        }
+        const int count = cast ? a.cellStart[r.cell + 1] - firstS[threadIdx.x] : 0;
+        // Block inclusive scan of the item counts.
+        {
+            int v = count;
+            const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+            for (int o = 1; o < 32; o <<= 1)
+            {
+                const int n = __shfl_up_sync(0xffffffffu, v, o);
+                if (lane >= o) v += n;
+            }
+            if (lane == 31) warpSumS[warp] = v;
+            __syncthreads();
+            if (warp == 0)
+            {
+                int t = lane < RESET_THREADS / 32 ? warpSumS[lane] : 0;
+                for (int o = 1; o < 32; o <<= 1)
+                {
+                    const int n = __shfl_up_sync(0xffffffffu, t, o);
+                    if (lane >= o) t += n;
+                }
+                if (lane < RESET_THREADS / 32) warpSumS[lane] = t;
+            }
+            __syncthreads();
+            endS[threadIdx.x] = v + (warp > 0 ? warpSumS[warp - 1] : 0);
+            __syncthreads();
+        }
+        const int items = endS[RESET_THREADS - 1];
+        for (int it = threadIdx.x; it < items; it += RESET_THREADS)
+        {
+            // Owner: the first thread whose inclusive end exceeds the item.
+            int lo = 0, hi = RESET_THREADS - 1;
+            while (lo < hi)
+            {
+                const int mid = (lo + hi) >> 1;
+                if (endS[mid] > it) hi = mid;
+                else lo = mid + 1;
+            }
+            const int cand = it - (lo > 0 ? endS[lo - 1] : 0);
+            const int tri = a.cellTris[firstS[lo] + cand];
+            const float4 p0 = a.triV[3 * tri], p1 = a.triV[3 * tri + 1], p2 = a.triV[3 * tri + 2];
+            const V3 v0 = { p0.x, p0.y, p0.z };
+            const V3 e1 = V3{ p1.x, p1.y, p1.z } - v0;
+            const V3 e2 = V3{ p2.x, p2.y, p2.z } - v0;
+            const V3 dir = { startS[12][lo], startS[13][lo], startS[14][lo] };
+            const V3 pv = cross(dir, e2);
+            const float det = dot(e1, pv);
+            if (fabsf(det) < RAY_PARALLEL_EPS) continue;
+            const float invDet = 1.f / det;
+            for (int w = 0; w < NUM_WHEELS; w++)
+            {
+                const V3 st = { startS[3 * w][lo], startS[3 * w + 1][lo], startS[3 * w + 2][lo] };
+                float d;
+                if (wheelTriHit(st, dir, v0, e1, e2, pv, invDet, suspRayLength(w) + 1.f, d))
+                    atomicMin(&keyS[w][lo], wheelKey(d, (unsigned)cand));
+            }
+        }
+        __syncthreads();
+        if (on)
+        {
+            float dist[NUM_WHEELS];
+            V3 normal[NUM_WHEELS];
+            int source[NUM_WHEELS];
+            if (demoed)
+            {
+                demoedWheelRays(dist, normal, source);
+            }
+            else
+            {
+                initWheelRays(r, dist, normal, source);
+                for (int w = 0; w < NUM_WHEELS; w++)
+                {
+                    const unsigned long long key = keyS[w][threadIdx.x];
+                    const unsigned cand = (unsigned)(key & 0xffffffffu);
+                    if (cand == 0xffffffffu) continue;
+                    const int tri = a.cellTris[firstS[threadIdx.x] + (int)cand];
+                    const float4 p0 = a.triV[3 * tri], p1 = a.triV[3 * tri + 1], p2 = a.triV[3 * tri + 2];
+                    const V3 v0 = { p0.x, p0.y, p0.z };
+                    V3 n = cross(V3{ p1.x, p1.y, p1.z } - v0, V3{ p2.x, p2.y, p2.z } - v0);
+                    const float nl = lensq(n);
+                    if (nl > 1e-12f)
+                    {
+                        dist[w] = __uint_as_float((unsigned)(key >> 32));
+                        source[w] = WHEEL_ARENA;
+                        n = n * rsqrtf(nl);
+                        if (dot(n, r.dir) > 0.f) n = neg(n);
+                        normal[w] = n;
+                    }
+                    else
+                    {
+                        // A degenerate winner keeps an earlier hit's normal: replay the serial pass.
+                        arenaRaysSerial(a, r, w, w + 1, dist, normal, source);
+                    }
+                }
+                carBallRays(g, car, sim, r, dist, normal, source);
+            }
+            storeRefresh(g, car, demoed, dist, normal, source);
+        }
+        __syncthreads();
+        // Obs rows through the warp's staging tile, one row per car thread.
+        {
+            WarpRowsAt e{ obsTile[warp], pk.obs + ((long long)sim * g.nCars + local) * pk.obsDim, lane, 0,
+                          __ballot_sync(0xffffffffu, on), pk.normalize != 0 };
+            emitObsRow(g, e, pk.invertOrange, pk.previousControls, sim, local);
+            e.finish();
+        }
+        if (on && local == 0)
+        {
+            packStateSim(g, pk.state, pk.stateDim, pk.tick, 1, sim);
+            packRawMatchSim(g, pk.outputs, sim);
+        }
+        __syncthreads();
+    }
 }
 
 inline int blocks(long long n, int t) { return (int)((n + t - 1) / t); }
@@ -645,11 +1089,20 @@ void launchResetDones(const GView& g, int tick, int maxTicks, int ot, int nt, cu
 void launchPackObs(const GView& g, float* out, const uint8_t* mask, int obsDim, bool invert, bool normalize, bool prev,
                    cudaStream_t s)
 {
-    packObsKernel<<<blocks((long long)g.nSim * g.nCars, 128), 128, 0, s>>>(g, out, mask, obsDim, invert, normalize, prev);
+    const long long n = (long long)g.nSim * g.nCars;
+    if (n <= 0) return;
+    if (g.stagedPack)
+        packObsWarpKernel<<<blocks(n, PACK_THREADS), PACK_THREADS, 0, s>>>(g, out, mask, obsDim, invert, normalize, prev);
+    else
+        packObsKernel<<<blocks(n, 128), 128, 0, s>>>(g, out, mask, obsDim, invert, normalize, prev);
 }
 void launchPackState(const GView& g, float* out, int stateDim, int tick, int touchWindow, const uint8_t* mask, cudaStream_t s)
 {
-    packStateKernel<<<blocks(g.nSim, 128), 128, 0, s>>>(g, out, stateDim, tick, touchWindow, mask);
+    if (g.nSim <= 0) return;
+    if (g.stagedPack)
+        packStateWarpKernel<<<blocks(g.nSim, PACK_THREADS), PACK_THREADS, 0, s>>>(g, out, stateDim, tick, touchWindow, mask);
+    else
+        packStateKernel<<<blocks(g.nSim, 128), 128, 0, s>>>(g, out, stateDim, tick, touchWindow, mask);
 }
 void launchPackRewardsDones(const GView& g, const Outputs& o, int tick, int maxTicks, int ot, int nt, cudaStream_t s)
 {
@@ -678,6 +1131,12 @@ void launchSetMatch(const GView& g, const int32_t* b, const int32_t* o, const in
 void launchResetPads(const GView& g, int n, const int64_t* idx, const uint8_t* mask, cudaStream_t s)
 {
     if (n > 0) resetPadsKernel<<<blocks(n, 128), 128, 0, s>>>(g, n, idx, mask);
+}
+void launchResetMasked(const GView& g, const ArenaDev& a, const BallInputs& ball, const CarInputs& cars,
+                       const MatchInputs& match, const uint8_t* mask, const PackTargets& pk, cudaStream_t s)
+{
+    if (g.nSim <= 0) return;
+    resetMaskedKernel<<<blocks(g.nSim, RESET_CHUNK), RESET_THREADS, 0, s>>>(g, a, ball, cars, match, mask, pk);
 }
 
 }  // namespace cb

@@ -18,6 +18,7 @@ struct GView
     int* simOut;         // [nSim] ball-arena contact tick (written by resets only)
     int nSim, nCars, nBlue, nOrange, seed;
     long long simOffset; // env-global index of sim 0
+    bool stagedPack;     // obs / state rows through per-warp staging tiles (coalesced stores)
 };
 
 struct Outputs
@@ -46,6 +47,21 @@ struct CarInputs
     const float* internal;               // [n, nCars, CAR_INTERNAL_SIZE] or null
 };
 
+struct MatchInputs
+{
+    const int32_t *blue, *orange, *ticks;  // [n] each, or all null
+};
+
+// Output buffers a masked reset repacks.
+struct PackTargets
+{
+    float* obs;
+    int obsDim, invertOrange, normalize, previousControls;
+    float* state;
+    int stateDim, tick;
+    Outputs outputs;
+};
+
 int uploadEnvioTables(const Tables& t);
 void launchClear(const GView& g, cudaStream_t s);
 void launchKickoff(const GView& g, int tick, cudaStream_t s);
@@ -63,5 +79,9 @@ void launchSetCar(const GView& g, const ArenaDev& a, const CarInputs& in, int n,
 void launchSetMatch(const GView& g, const int32_t* blue, const int32_t* orange, const int32_t* ticks, int n,
                     const int64_t* idx, const uint8_t* mask, cudaStream_t s);
 void launchResetPads(const GView& g, int n, const int64_t* idx, const uint8_t* mask, cudaStream_t s);
+// Masked apply_reset_state (all sims with mask[sim] != 0, input row = sim) and
+// the repacking of their obs, state and raw match outputs, in one launch.
+void launchResetMasked(const GView& g, const ArenaDev& a, const BallInputs& ball, const CarInputs& cars,
+                       const MatchInputs& match, const uint8_t* mask, const PackTargets& pk, cudaStream_t s);
 
 }  // namespace cb

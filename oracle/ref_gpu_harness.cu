@@ -382,6 +382,84 @@ int carlrefgpu_tick_partial(void* h, int kind, const void* actions, int lastStag
     return 0;
 }
 
+/* Times `nSteps` env steps (python/carl.cu:312-370, frameskip ticks + packing),
+ * each followed by the masked apply_reset_state sequence of python/carl.cu:508-666
+ * (pads, ball, cars with contact refresh, match state, obs / state / raw match
+ * repack of the masked sims) with masks[step * n_sim ...]; with masks NULL the
+ * steps run alone.  Actions and reset inputs (one row per sim, kickoff states
+ * for instance) are staged once; device time of the steps and of the resets is
+ * summed separately (milliseconds). */
+int carlrefgpu_time_reset_steps(
+    void* h, int kind, const void* actions, int nSteps,
+    const float* ballPos, const float* ballVel, const float* ballAng,
+    const float* carPos, const float* carRot, const float* carVel, const float* carAng,
+    const uint8_t* demoed, const int32_t* blue, const int32_t* orange, const int32_t* ticks,
+    const uint8_t* masks, float* stepMs, float* resetMs)
+{
+    auto* e = static_cast<RefGpu*>(h);
+    cudaStream_t s = e->env.getStream();
+    const int nCars = e->env.getNCars();
+    const int nSim = e->env.getNSim();
+    const size_t v3 = (size_t)nSim * 3 * 4, c3 = (size_t)nSim * nCars * 3 * 4;
+    HCHECK(e->actions.assign(actions, actionBytes(kind, nSim * nCars), s));
+    DeviceBuffer* b = e->staging;
+    HCHECK(b[0].assign(ballPos, v3, s));
+    HCHECK(b[1].assign(ballVel, v3, s));
+    HCHECK(b[2].assign(ballAng, v3, s));
+    HCHECK(b[3].assign(carPos, c3, s));
+    HCHECK(b[4].assign(carRot, (size_t)nSim * nCars * 4 * 4, s));
+    HCHECK(b[5].assign(carVel, c3, s));
+    HCHECK(b[6].assign(carAng, c3, s));
+    HCHECK(b[7].assign(demoed, (size_t)nSim * nCars, s));
+    HCHECK(b[12].assign(blue, (size_t)nSim * 4, s));
+    HCHECK(b[13].assign(orange, (size_t)nSim * 4, s));
+    HCHECK(b[14].assign(ticks, (size_t)nSim * 4, s));
+    if (masks) HCHECK(b[15].assign(masks, (size_t)nSteps * nSim, s));
+    HCHECK(cudaStreamSynchronize(s));
+    cudaEvent_t mid = nullptr;
+    HCHECK(cudaEventCreate(&mid));
+    float stepTotal = 0.f, resetTotal = 0.f;
+    for (int step = 0; step < nSteps; step++)
+    {
+        GameState* ds = e->env.getDeviceState();
+        cudaEventRecord(e->start, s);
+        e->envStep(kind);
+        cudaEventRecord(mid, s);
+        if (masks)
+        {
+        const bool* dMask = reinterpret_cast<const bool*>(static_cast<const uint8_t*>(b[15].ptr) + (size_t)step * nSim);
+        e->io.resetBoostPads(ds, nullptr, nSim, dMask);
+        e->io.setBall(ds, (const float*)b[0].ptr, (const float*)b[1].ptr, (const float*)b[2].ptr, nullptr, nSim, dMask);
+        e->io.setCar(ds, e->env.getDeviceWorkspace(), e->env.getDeviceArena(),
+                     (const float*)b[3].ptr, (const float*)b[4].ptr, (const float*)b[5].ptr,
+                     (const float*)b[6].ptr, b[7].ptr, true, nullptr, nullptr, nullptr, nSim, dMask);
+        e->io.setMatchState(ds, (const int32_t*)b[12].ptr, (const int32_t*)b[13].ptr, (const int32_t*)b[14].ptr,
+                            nullptr, nSim, dMask);
+        e->io.packObs(ds, dMask);
+        e->io.packState(ds, dMask);
+        e->io.packRawMatchState(ds, dMask);
+        }
+        cudaEventRecord(e->stop, s);
+        const cudaError_t err = cudaEventSynchronize(e->stop);
+        if (err != cudaSuccess)
+        {
+            cudaEventDestroy(mid);
+            g_error = cudaGetErrorString(err);
+            return 1;
+        }
+        float a = 0.f, c = 0.f;
+        cudaEventElapsedTime(&a, e->start, mid);
+        cudaEventElapsedTime(&c, mid, e->stop);
+        stepTotal += a;
+        resetTotal += c;
+    }
+    cudaEventDestroy(mid);
+    HCHECK(cudaGetLastError());
+    *stepMs = stepTotal;
+    *resetMs = resetTotal;
+    return 0;
+}
+
 /* apply_reset_state (python/carl.cu:508-666) with host inputs; NULL for the
  * optional ones.  demoed is u8 when demoedIsByte, else int32. */
 int carlrefgpu_apply_reset_state(

@@ -65,6 +65,8 @@ def _load(kind: str) -> ctypes.CDLL:
         lib.carlrefgpu_tick_partial.argtypes = [vp, i32, vp, i32]
         lib.carlrefgpu_time_ticks.argtypes = [vp, i32, vp, i32, ctypes.POINTER(ctypes.c_float)]
         lib.carlrefgpu_apply_reset_state.argtypes = [vp, i32] + [vp] * 8 + [i32] + [vp] * 7
+        lib.carlrefgpu_time_reset_steps.argtypes = ([vp, i32, vp, i32] + [vp] * 12
+                                                    + [ctypes.POINTER(ctypes.c_float)] * 2)
     _libs[kind] = lib
     return lib
 
@@ -195,6 +197,21 @@ class RefGpu(_RefEnv):
         ms = ctypes.c_float()
         self._call("time_ticks", kind, np.ascontiguousarray(actions).ctypes.data, n_ticks, ctypes.byref(ms))
         return ms.value
+
+    def time_reset_steps(self, kind: int, actions: np.ndarray, n_steps: int, reset: dict | None = None,
+                         masks: np.ndarray | None = None) -> tuple[float, float]:
+        """Device ms of n_steps env steps and of the masked resets after each
+        (reset: one row per sim of every apply_reset_state input, demoed u8;
+        masks [n_steps, n_sim]); without masks the steps run alone."""
+        step_ms, reset_ms = ctypes.c_float(), ctypes.c_float()
+        order = ["ball_position", "ball_velocity", "ball_angular_velocity", "car_position", "car_rotation",
+                 "car_velocity", "car_angular_velocity", "car_demoed", "blue_score", "orange_score", "episode_ticks"]
+        arrs = [None if reset is None else np.ascontiguousarray(reset[o]) for o in order]
+        masks = None if masks is None else np.ascontiguousarray(masks, dtype=np.uint8)
+        actions = np.ascontiguousarray(actions)
+        self._call("time_reset_steps", kind, actions.ctypes.data, n_steps, *[_addr(a) for a in arrs],
+                   _addr(masks), ctypes.byref(step_ms), ctypes.byref(reset_ms))
+        return step_ms.value, reset_ms.value
 
     def apply_reset_state(self, n_selected, ball_position, ball_velocity, ball_angular_velocity, car_position,
                           car_rotation, car_velocity, car_angular_velocity, car_demoed, demoed_is_byte,

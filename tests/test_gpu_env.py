@@ -204,6 +204,9 @@ def test_apply_reset_state_matches_reference_cuda_build(oracle_built, mode):
     env.synchronize()
     rep = parity.compare_snapshots(env.snapshot(), ref.snapshot())
     assert parity.all_ok(rep), parity.summarize(rep)
+    # The outputs the reset repacks (the masked path: one fused kernel).
+    for b in [capi.BUF_OBS, capi.BUF_STATE, capi.BUF_SCORE_DIFFERENCE, capi.BUF_EPISODE_TICKS, capi.BUF_OVERTIME]:
+        assert buffers_close(read_buffer(env, b), ref.get_buffer(b)) == 0, b
     ctl = workloads.controls(rng, n_sim * n_cars)
     env.ticks(capi.ACTIONS_DIRECT, t.from_numpy(ctl.view(np.int32)).cuda(), 1)
     ref.ticks(capi.ACTIONS_DIRECT, ctl, 1)
