@@ -84,9 +84,9 @@ def parse_args():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--workload", choices=["c3", "step", "reset"], default="c3",
+    ap.add_argument("--workload", choices=["c3", "step", "reset", "mask"], default="c3",
                     help="c3: the headline tick throughput; step: env steps at frameskip 8 (ticks + packing); "
-                         "reset: env steps with masked resets (C5 shard)")
+                         "reset: env steps with masked resets (C5 shard); mask: device action masks")
     ap.add_argument("--reset-n-sim", type=int, default=131072, help="sims of the reset workload (4v4)")
     return ap.parse_args()
 
@@ -589,6 +589,69 @@ def run_env_workload(args, resets: bool) -> None:
     print(json.dumps(line), flush=True)
 
 
+def reference_action_mask(observation, previous_controls: bool):
+    """The reference's own mask (python/carl/gymnasium/action.py:17-37), the torch
+    op chain the device kernel replaces; timed as that row's reference arm."""
+    import torch as th
+
+    from carl_b200 import carl
+
+    size = carl.OBS_PREVIOUS_CONTROLS if previous_controls else 0
+    on_ground = observation[..., carl.OBS_EGO_ON_GROUND_INDEX].bool()
+    has_boost = observation[..., carl.OBS_EGO_BOOST_INDEX].gt(0)
+    flip_available = observation[..., carl.OBS_EGO_FLIP_INDEX - size].bool()
+    jump_available = on_ground | (flip_available & (observation[..., carl.OBS_EGO_DODGE_TIME_INDEX - size] > carl.PHYS_DT))
+    mask = th.ones((*observation.shape[:-1], carl.ACTION_LOGITS), dtype=th.bool, device=observation.device)
+    mask[..., carl.ACTION_POWERSLIDE_LOGIT] = on_ground
+    mask[..., carl.ACTION_BOOST_LOGIT] = has_boost
+    mask[..., carl.ACTION_JUMP_LOGIT] = jump_available
+    return mask
+
+
+def run_mask_workload(args) -> None:
+    """Action masks of a packed observation batch (config C5's per-GPU shard:
+    4v4, --reset-n-sim sims): the device kernel (carl_b200.action.CARLActionCodec)
+    against the reference's torch op chain, both on torch's current stream,
+    CUDA-event timed, results checked equal."""
+    import torch
+
+    from carl_b200 import carl, workloads
+    from carl_b200.action import CARLActionCodec
+
+    n_sim = args.reset_n_sim
+    env = carl.Env(n_sim, 4, 4, args.seed)
+    workloads.mixed_state(env._env, args.seed)
+    rng = np.random.default_rng(args.seed + 9)
+    obs = env.step(torch.from_numpy(workloads.discrete_actions(rng, n_sim * 8).reshape(n_sim, 8, 7)).cuda())
+    torch.cuda.current_stream().wait_stream(torch.cuda.ExternalStream(env.stream))
+    codec = CARLActionCodec()
+    assert torch.equal(codec.mask(obs), reference_action_mask(obs, False))
+    out = {}
+    for name, fn in (("b200", codec.mask), ("reference_torch", lambda o: reference_action_mask(o, False))):
+        for _ in range(args.warmup):
+            fn(obs)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            fn(obs)
+        end.record()
+        end.synchronize()
+        out[name] = {"ms": start.elapsed_time(end) / args.steps}
+    rows = n_sim * 8
+    for r in out.values():
+        r["rows_per_s"] = rows / (r["ms"] / 1e3)
+    line = {
+        "metric": "action-mask rows/sec", "value": out["b200"]["rows_per_s"], "unit": "rows/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": out["b200"]["ms"], "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (obs packed from seeded C4 mixed states after one env step)",
+        "config": {"workload": f"CARLActionCodec.mask of [{n_sim}, 8, {obs.shape[-1]}] observations (C5 shard)"},
+        "modes": out,
+    }
+    print(json.dumps(line), flush=True)
+    env.close()
+
+
 def main():
     args = parse_args()
     rank = int(os.environ.get("RANK", "0"))
@@ -597,6 +660,10 @@ def main():
     if args.workload in ("reset", "step"):
         if rank == 0:
             run_env_workload(args, resets=args.workload == "reset")
+        return
+    if args.workload == "mask":
+        if rank == 0:
+            run_mask_workload(args)
         return
     if args.impl == "reference":
         run_reference(args, rank, world)

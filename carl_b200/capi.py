@@ -119,6 +119,7 @@ def load() -> ctypes.CDLL:
     lib.carlb_last_tick_ms.argtypes = [vp, ctypes.POINTER(ctypes.c_float)]
     lib.carlb_set_stage_timing.argtypes = [vp, i32]
     lib.carlb_stage_times.argtypes = [vp, ctypes.POINTER(ctypes.c_float), i32, ctypes.POINTER(i32)]
+    lib.carlb_action_mask.argtypes = [vp, i64, i32, i32, vp, vp]
     _lib = lib
     return lib
 
@@ -132,6 +133,15 @@ def _ptr(x) -> int | None:
     if isinstance(x, np.ndarray):
         return x.ctypes.data
     return x.data_ptr()
+
+
+def action_mask(obs, rows: int, obs_dim: int, previous_controls: bool, mask, stream: int) -> None:
+    """carlb_action_mask: uint8 [rows, 18] action mask of float32 [rows, obs_dim]
+    observation rows (device addresses or tensors), enqueued on `stream`."""
+    lib = load()
+    st = lib.carlb_action_mask(_ptr(obs), rows, obs_dim, int(previous_controls), _ptr(mask), stream)
+    if st != OK:
+        raise CarlbError(st, lib.carlb_last_error(None).decode())
 
 
 class Env:

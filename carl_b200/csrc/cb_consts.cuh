@@ -243,6 +243,11 @@ constexpr int ACT_PER_CAR = 7;
 constexpr int ACTION_NVECS[ACT_PER_CAR] = { 3, 3, 3, 2, 2, 3, 2 };
 constexpr int ACTION_LOGITS = 18;
 constexpr int ACT_NON_NEUTRAL = 1;
+// Logit columns the action mask gates (python/carl.cu:825-909 ACTION_*_LOGIT:
+// the non-neutral logit of powerslide, boost and jump).
+constexpr int ACTION_POWERSLIDE_LOGIT = 3 + 3 + 3 + 1;
+constexpr int ACTION_BOOST_LOGIT = 3 + 3 + 3 + 2 + 1;
+constexpr int ACTION_JUMP_LOGIT = 3 + 3 + 3 + 2 + 2 + 3 + 1;
 
 // ---- curves ----
 CB_HD float steerAngleFromSpeed(float x)

@@ -1063,6 +1063,22 @@ carlb_status carlb_last_tick_ms(const carlb_env* e, float* ms)
     return err == cudaSuccess ? CARLB_OK : CARLB_ERR_CUDA;
 }
 
+carlb_status carlb_action_mask(const float* obs, int64_t rows, int32_t obsDim, int32_t previousControls,
+                               uint8_t* mask, void* stream)
+{
+    if (rows < 0) return fail(nullptr, CARLB_ERR_VALUE, "rows must be non-negative");
+    if (rows == 0) return CARLB_OK;
+    if (!obs || !mask) return fail(nullptr, CARLB_ERR_VALUE, "obs and mask must not be null");
+    if (reinterpret_cast<uintptr_t>(mask) % 4 != 0) return fail(nullptr, CARLB_ERR_VALUE, "mask must be 4-byte aligned");
+    const int controls = previousControls ? OBS_PREVIOUS_CONTROLS : 0;
+    if (obsDim < OBS_BALL + OBS_PER_CAR - OBS_EGO_FLIP_INDEX + controls)
+        return fail(nullptr, CARLB_ERR_VALUE, "obs_dim is too small for an observation row");
+    launchActionMask(obs, rows, obsDim, previousControls != 0, mask, (cudaStream_t)stream);
+    const cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) return fail(nullptr, CARLB_ERR_CUDA, std::string("action mask: ") + cudaGetErrorString(err));
+    return CARLB_OK;
+}
+
 carlb_status carlb_set_diagnostics(carlb_env* e, int32_t enabled)
 {
     if (!e) return fail(nullptr, CARLB_ERR_VALUE, "env is null");

@@ -209,9 +209,7 @@ struct WarpRows
     {
         if (k & 31) flush(k & 31);
     }
-    // Out of line: a row emits hundreds of values, and an inlined flush at every
-    // emit would bloat the kernel past the instruction cache.
-    __device__ __noinline__ void flush(int n)
+    __device__ void flush(int n)
     {
         __syncwarp();
         const int c0 = k - n;
@@ -855,9 +853,7 @@ struct WarpRowsAt
     {
         if (k & 31) flush(k & 31);
     }
-    // Out of line: a row emits hundreds of values, and an inlined flush at every
-    // emit would bloat the kernel past the instruction cache.
-    __device__ __noinline__ void flush(int n)
+    __device__ void flush(int n)
     {
         __syncwarp();
         const int c0 = k - n;
@@ -1070,6 +1066,53 @@ __global__ void __launch_bounds__(RESET_THREADS) resetMaskedKernel(GView g, Aren
     }
 }
 
+// Action mask of each observation row (python/carl/gymnasium/action.py:17-37,
+// CARLActionCodec.mask): every logit allowed except powerslide (on ground),
+// boost (boost > 0) and jump (on ground, or a flip available with more than one
+// tick of dodge window left).  Flags read as the reference's torch ops do:
+// `.bool()` is `!= 0` (NaN counts as set), comparisons are false for NaN.
+// A warp's 32 mask rows are 576 contiguous bytes: they are assembled in shared
+// memory and written as 144 four-byte words (the mask must be 4-byte aligned;
+// a warp holding the last rows writes bytes).
+constexpr int MASK_THREADS = 256;
+
+__global__ void __launch_bounds__(MASK_THREADS) actionMaskKernel(const float* obs, long long rows, int obsDim,
+                                                                 int controlsSize, uint8_t* mask)
+{
+    __shared__ __align__(4) uint8_t rowsS[MASK_THREADS / 32][32 * ACTION_LOGITS];
+    const long long r = blockIdx.x * (long long)MASK_THREADS + threadIdx.x;
+    const int lane = threadIdx.x & 31;
+    uint8_t* m = rowsS[threadIdx.x >> 5] + lane * ACTION_LOGITS;
+    if (r < rows)
+    {
+        const float* o = obs + r * obsDim;
+        const bool onGround = o[OBS_BALL + OBS_ON_GROUND] != 0.f;
+        const bool hasBoost = o[OBS_BALL + OBS_BOOST] > 0.f;
+        const bool flipAvailable = o[obsDim + OBS_EGO_FLIP_INDEX - controlsSize] != 0.f;
+        const bool jump = onGround || (flipAvailable && o[obsDim + OBS_EGO_DODGE_TIME_INDEX - controlsSize] > PHYS_DT);
+        for (int k = 0; k < ACTION_LOGITS; k++) m[k] = 1;
+        m[ACTION_POWERSLIDE_LOGIT] = onGround;
+        m[ACTION_BOOST_LOGIT] = hasBoost;
+        m[ACTION_JUMP_LOGIT] = jump;
+    }
+    __syncwarp();
+    const long long r0 = r - lane;
+    if (r0 >= rows) return;
+    const long long n = rows - r0 < 32 ? rows - r0 : 32;
+    uint8_t* dst = mask + r0 * ACTION_LOGITS;
+    const uint8_t* src = rowsS[threadIdx.x >> 5];
+    if (n == 32)
+    {
+        const unsigned* s32 = reinterpret_cast<const unsigned*>(src);
+        unsigned* d32 = reinterpret_cast<unsigned*>(dst);
+        for (int w = lane; w < 32 * ACTION_LOGITS / 4; w += 32) d32[w] = s32[w];
+    }
+    else
+    {
+        for (int b = lane; b < n * ACTION_LOGITS; b += 32) dst[b] = src[b];
+    }
+}
+
 inline int blocks(long long n, int t) { return (int)((n + t - 1) / t); }
 
 }  // namespace
@@ -1131,6 +1174,13 @@ void launchSetMatch(const GView& g, const int32_t* b, const int32_t* o, const in
 void launchResetPads(const GView& g, int n, const int64_t* idx, const uint8_t* mask, cudaStream_t s)
 {
     if (n > 0) resetPadsKernel<<<blocks(n, 128), 128, 0, s>>>(g, n, idx, mask);
+}
+void launchActionMask(const float* obs, long long rows, int obsDim, bool previousControls, uint8_t* mask, cudaStream_t s)
+{
+    if (rows > 0)
+        actionMaskKernel<<<blocks(rows, MASK_THREADS), MASK_THREADS, 0, s>>>(obs, rows, obsDim,
+                                                                            previousControls ? OBS_PREVIOUS_CONTROLS : 0,
+                                                                            mask);
 }
 void launchResetMasked(const GView& g, const ArenaDev& a, const BallInputs& ball, const CarInputs& cars,
                        const MatchInputs& match, const uint8_t* mask, const PackTargets& pk, cudaStream_t s)

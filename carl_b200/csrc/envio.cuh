@@ -79,6 +79,9 @@ void launchSetCar(const GView& g, const ArenaDev& a, const CarInputs& in, int n,
 void launchSetMatch(const GView& g, const int32_t* blue, const int32_t* orange, const int32_t* ticks, int n,
                     const int64_t* idx, const uint8_t* mask, cudaStream_t s);
 void launchResetPads(const GView& g, int n, const int64_t* idx, const uint8_t* mask, cudaStream_t s);
+// Action mask rows [rows, ACTION_LOGITS] (u8) of observation rows [rows, obsDim].
+void launchActionMask(const float* obs, long long rows, int obsDim, bool previousControls, uint8_t* mask,
+                      cudaStream_t s);
 // Masked apply_reset_state (all sims with mask[sim] != 0, input row = sim) and
 // the repacking of their obs, state and raw match outputs, in one launch.
 void launchResetMasked(const GView& g, const ArenaDev& a, const BallInputs& ball, const CarInputs& cars,

@@ -298,6 +298,18 @@ carlb_status carlb_set_stage_timing(carlb_env* env, int32_t enabled);
  * solve, car-car, ball arena, finish.  Waits for that tick to complete. */
 carlb_status carlb_stage_times(carlb_env* env, float* ms, int32_t capacity, int32_t* count);
 
+/* Action mask of observation rows, on the device: obs is float32 [rows, obs_dim]
+ * (device memory, row-major), mask receives uint8 [rows, 18] (1 = logit allowed),
+ * enqueued on `stream` (a cudaStream_t; NULL = the legacy default stream).
+ * previous_controls says whether the rows end with the 8 previous-control values.
+ * Replaces python/carl/gymnasium/action.py:17-37 (CARLActionCodec.mask, a chain of
+ * torch ops): all logits allowed except powerslide (ego on ground), boost (ego
+ * boost > 0) and jump (on ground, or a flip available with more than PHYS_DT of
+ * dodge window left).  CARLB_ERR_VALUE for a null pointer with rows > 0, negative
+ * rows, a mask that is not 4-byte aligned, or obs_dim too small for the ego fields. */
+carlb_status carlb_action_mask(const float* obs, int64_t rows, int32_t obs_dim, int32_t previous_controls,
+                               uint8_t* mask, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
