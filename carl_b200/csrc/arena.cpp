@@ -24,6 +24,43 @@ std::string arenaObjPath(const std::string& fallback)
     return fallback;
 }
 
+std::string arenaMetadataPath()
+{
+    const char* env = std::getenv("CARL_ARENA_METADATA");
+    return env ? std::string(env) : std::string();
+}
+
+std::string loadNativeMetadata(const std::string& path, ArenaHost& a)
+{
+    std::ifstream file(path);
+    if (!file.is_open()) return "cannot open CARL arena metadata '" + path + "'";
+    const int nTris = a.nTris();
+    int count = 0;
+    file >> count;
+    if (count != nTris) return "CARL arena metadata triangle count mismatch";
+    a.nativeMesh.assign(nTris, 0);
+    a.nativeOrder.assign(nTris, 0);
+    a.nativeFlags.assign(nTris, 0);
+    a.nativeAngles.assign((size_t)nTris * 3, 0.f);
+    a.nativeVerts.assign((size_t)nTris * 9, 0.f);
+    for (int t = 0; t < nTris; t++)
+    {
+        file >> a.nativeMesh[t] >> a.nativeOrder[t];
+        for (int k = 0; k < 3; k++) file >> a.nativeAngles[3 * t + k];
+        file >> a.nativeFlags[t];
+        for (int k = 0; k < 9; k++) file >> a.nativeVerts[9 * t + k];
+    }
+    if (!file) return "Invalid CARL arena metadata";
+    a.hasNative = true;
+    // Ball-cell lists in traversal-key order; equal keys keep ascending triangle
+    // order (a stable sort of the ascending lists).
+    const size_t nb = a.ballCellStart.size() - 1;
+    for (size_t c = 0; c < nb; c++)
+        std::stable_sort(a.ballCellTris.begin() + a.ballCellStart[c], a.ballCellTris.begin() + a.ballCellStart[c + 1],
+                         [&](int x, int y) { return a.ballKey(x) < a.ballKey(y); });
+    return "";
+}
+
 namespace {
 
 uint32_t weldBits(float v)

@@ -43,9 +43,31 @@ struct ArenaHost
     std::vector<int32_t> ballCellStart;  // [ballDims product + 1]
     std::vector<int32_t> ballCellTris;   // [ballCellStart.back()]
 
+    // Native mesh metadata ($CARL_ARENA_METADATA, src/ArenaMesh.cu:69-99): per
+    // triangle its native mesh (negative: no ball contact) and traversal order
+    // within it, its edge angles and edge flags in the native mesh, and its
+    // vertices in Bullet units.  With it the ball's arena contacts take the
+    // native branch, and every ball-cell list is ordered by the traversal key
+    // mesh * 10000 + order (the order the reference merges its cell lists in).
+    bool hasNative = false;
+    std::vector<int32_t> nativeMesh, nativeOrder, nativeFlags;  // [nTris]
+    std::vector<float> nativeAngles;                            // [nTris][3]
+    std::vector<float> nativeVerts;                             // [nTris][3 vertices][3]
+
     int nVerts() const { return (int)verts.size() / 3; }
     int nTris() const { return (int)tris.size() / 3; }
+    // Traversal key of a triangle for the ball (triangle index without metadata).
+    int32_t ballKey(int t) const { return hasNative ? nativeMesh[t] * 10000 + nativeOrder[t] : t; }
 };
+
+// Path of the native metadata file: $CARL_ARENA_METADATA, or empty.
+std::string arenaMetadataPath();
+
+// Reads the native metadata file (format of src/ArenaMesh.cu:69-99: the triangle
+// count, then per triangle `mesh order a0 a1 a2 flags` and its three vertices)
+// into `a` and reorders the ball-cell lists by traversal key.  Returns an empty
+// string on success, else the error (the reference's messages).
+std::string loadNativeMetadata(const std::string& path, ArenaHost& a);
 
 // Path of the arena mesh: $CARL_ARENA_OBJ if set, else `fallback`.
 std::string arenaObjPath(const std::string& fallback);

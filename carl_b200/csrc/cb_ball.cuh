@@ -4,7 +4,7 @@
 // and solver, the "extra hit" impulse, Bullet-unit integration and goals.
 //
 // Follows jwmccarthy/CARL include/Physics/BallArena/{Contact,Solver,Solve}.cuh
-// (default arena path, no native mesh metadata), include/Physics/CarBall/
+// (the default arena path and the native-metadata path), include/Physics/CarBall/
 // {Contact,Solve,ExtraImpulse}.cuh and include/Physics/Goals.cuh:6-32, with the
 // same fp32 operation order.  The arena triangles near the ball are visited in
 // ascending triangle order, as the reference's per-cell merge does.
@@ -165,6 +165,123 @@ CB_D void insertBallContact(BallContact* set, int& count, BallContact c, V3 cent
     set[slot] = c;
 }
 
+// ---- native mesh branch ------------------------------------------------------------------------
+// With native mesh metadata (src/ArenaMesh.cu:69-99) the ball meets the arena in
+// Bullet units against the native triangles (BallArena/Contact.cuh:161-201,
+// 292-343, 478-593): contacts are reduced to four per native mesh, the edge
+// correction uses the native angles and edge flags, and the four arena planes
+// are added as contacts after the mesh contacts are scaled back to Unreal units.
+
+constexpr int MAX_BALL_ARENA_CONTACTS = 68;  // four per native mesh (16 meshes) plus the four planes
+
+// Sphere (the ball in Bullet units, centre `center`) against a native triangle.
+CB_D bool nativeSphereTriangle(V3 center, V3 v0, V3 v1, V3 v2, BallContact& c)
+{
+    constexpr float radius = BALL_COLLISION_RADIUS * .02f;
+    constexpr float extent = radius + BALL_ARENA_CONTACT_BREAK * .02f;
+    const V3 e01 = v1 - v0, e02 = v2 - v0, off = center - v0;
+    const V3 fn = cross(e01, e02);
+    const float nl = lensq(fn);
+    if (nl < 1e-14f) return false;
+    V3 normal = fn * (1.f / sqrtf(nl));
+    float planeDist = dot(off, normal);
+    if (planeDist < 0.f)
+    {
+        planeDist = -planeDist;
+        normal = neg(normal);
+    }
+    if (planeDist >= extent) return false;
+    // Barycentric coordinates of the centre's projection.
+    const float gamma = dot(cross(e01, off), fn) / nl;
+    const float beta = dot(cross(off, e02), fn) / nl;
+    const float alpha = 1.f - gamma - beta;
+    const bool inside = alpha >= 0.f && alpha <= 1.f && beta >= 0.f && beta <= 1.f && gamma >= 0.f && gamma <= 1.f;
+    c.point = inside ? center - normal * planeDist : closestPointOnTriangle(center, v0, v1, v2);
+    const V3 delta = center - c.point;
+    const float distSq = lensq(delta);
+    if (distSq >= extent * extent) return false;
+    const float distance = sqrtf(distSq);
+    c.normal = distSq > FLOAT_EPSILON ? delta * (1.f / distance) : normal;
+    c.depth = distSq > FLOAT_EPSILON ? radius - distance : radius;
+    c.relPos = (c.point - c.normal * c.depth) - center;
+    return true;
+}
+
+// Internal-edge correction of a native contact (point and normal in Bullet
+// units).  Edge e runs v_e -> v_(e+1)%3; flag bit e says the face normal points
+// to the positive side of its edge, bit e + 3 that the neighbour's normal is
+// flipped; a zero angle marks a concave edge.
+CB_D void adjustNativeBallEdgeNormal(BallContact& c, V3 v0, V3 v1, V3 v2, V3 angles, int flags)
+{
+    constexpr float edgeDistance = .1f;
+    const V3 verts[3] = { v0, v1, v2 };
+    int bestEdge = -1;
+    float bestDistSq = edgeDistance * edgeDistance;
+    for (int e = 0; e < 3; e++)
+    {
+        if (fabsf(vget(angles, e)) >= BOUNDARY_EDGE_ANGLE) continue;
+        const V3 start = verts[e];
+        const V3 edge = verts[(e + 1) % 3] - start;
+        const float t = clampf(dot(c.point - start, edge) / lensq(edge), 0.f, 1.f);
+        const V3 nearest = start + edge * t;
+        const float d = lensq(c.point - nearest);
+        if (d < bestDistSq)
+        {
+            bestDistSq = d;
+            bestEdge = e;
+        }
+    }
+    if (bestEdge < 0) return;
+
+    const V3 faceNormal = normalized(cross(v1 - v0, v2 - v0));
+    const V3 edgeDir = normalized(verts[bestEdge] - verts[(bestEdge + 1) % 3]);
+    const float angle = vget(angles, bestEdge);
+    bool concave = angle == 0.f;
+    if (!concave)
+    {
+        const float sign = (flags & (1 << bestEdge)) ? 1.f : -1.f;
+        V3 other = rotateAbout(faceNormal, edgeDir, angle);
+        if (flags & (1 << (bestEdge + 3))) other = neg(other);
+        concave = dot(c.normal, faceNormal * sign) < 0.f && dot(c.normal, other * sign) < 0.f;
+        if (!concave)
+        {
+            V3 clamped;
+            if (clampEdgeNormal(edgeDir, faceNormal * sign, c.normal, angle, clamped) && dot(clamped, faceNormal) > 0.f)
+                c.normal = clamped;
+        }
+    }
+    if (concave && dot(faceNormal, c.normal) >= 0.f) c.normal = faceNormal;
+}
+
+// Scales the native contacts back to Unreal units and adds a contact for each
+// arena plane (floor, ceiling, the two side walls) within the contact break.
+CB_D int finishNativeBallContacts(BallContact* set, int count, V3 center)
+{
+    for (int i = 0; i < count; i++)
+    {
+        set[i].point = set[i].point * 50.f;
+        set[i].relPos = set[i].relPos * 50.f;
+        set[i].depth *= 50.f;
+    }
+    const V3 normals[4] = { V3{ 0.f, 0.f, 1.f }, V3{ 0.f, 0.f, -1.f }, V3{ 1.f, 0.f, 0.f }, V3{ -1.f, 0.f, 0.f } };
+    const float offsets[4] = { 0.f, -2044.f, -4096.f, -4096.f };
+    for (int k = 0; k < 4; k++)
+    {
+        const float depth = BALL_COLLISION_RADIUS - (dot(normals[k], center) - offsets[k]);
+        if (depth > -BALL_ARENA_CONTACT_BREAK && count < MAX_BALL_ARENA_CONTACTS)
+        {
+            BallContact c;
+            c.point = center - normals[k] * (BALL_COLLISION_RADIUS - depth);
+            c.relPos = normals[k] * -BALL_COLLISION_RADIUS;
+            c.normal = normals[k];
+            c.depth = depth;
+            c.tri = -1;
+            set[count++] = c;
+        }
+    }
+    return count;
+}
+
 // ---- ball-arena solver ----------------------------------------------------------------------------
 
 struct BallRow
@@ -230,10 +347,12 @@ CB_D void clampBallVelocity(V3& vel, V3& ang)
     if (a2 > BALL_MAX_ANG_SPEED * BALL_MAX_ANG_SPEED) ang = ang * (BALL_MAX_ANG_SPEED * rsqrtf(a2));
 }
 
-CB_D void solveBallArena(BallBody& b, const BallContact* c, int count, bool ballWasHit)
+// Averaged-contact solve of `count` (<= CAP) contacts.
+template <int CAP>
+CB_D void solveBallArenaN(BallBody& b, const BallContact* c, int count, bool ballWasHit)
 {
     if (count == 0) return;
-    BallRow split[4];
+    BallRow split[CAP];
     V3 totalNormal = v3zero();
     float totalRadius = 0.f;
     const bool splitCorrection = !ballWasHit || count != 1 || c[0].normal.z < 0.999f;
@@ -278,6 +397,11 @@ CB_D void solveBallArena(BallBody& b, const BallContact* c, int count, bool ball
     b.vel = b.vel + b.deltaVel;
     b.ang = b.ang + b.deltaAng;
     clampBallVelocity(b.vel, b.ang);
+}
+
+CB_D void solveBallArena(BallBody& b, const BallContact* c, int count, bool ballWasHit)
+{
+    solveBallArenaN<4>(b, c, count, ballWasHit);
 }
 
 // ---- ball vs car -----------------------------------------------------------------------------------

@@ -41,18 +41,20 @@ std::string libraryDir()
     return ".";
 }
 
-// Host arena tables, built once per process and path.
-std::shared_ptr<const ArenaHost> hostArena(const std::string& path, std::string& err)
+// Host arena tables, built once per process, mesh path and metadata path.
+std::shared_ptr<const ArenaHost> hostArena(const std::string& path, const std::string& metadata, std::string& err)
 {
     static std::mutex mu;
     static std::map<std::string, std::shared_ptr<const ArenaHost>> cache;
     std::lock_guard<std::mutex> lock(mu);
-    auto it = cache.find(path);
+    const std::string key = path + '\n' + metadata;
+    auto it = cache.find(key);
     if (it != cache.end()) return it->second;
     auto a = std::make_shared<ArenaHost>();
     err = buildArena(path, *a);
+    if (err.empty() && !metadata.empty()) err = loadNativeMetadata(metadata, *a);
     if (!err.empty()) return nullptr;
-    cache[path] = a;
+    cache[key] = a;
     return a;
 }
 
@@ -85,6 +87,8 @@ struct carlb_env
     int* ballCellStart = nullptr;
     int* ballCellTris = nullptr;
     float4* ballCellSph = nullptr;
+    int hasNative = 0;
+    float4 *nativeV = nullptr, *nativeAng = nullptr;
     float carReach = 0.f;
     int* cellStart = nullptr;
     int* cellTris = nullptr;
@@ -172,7 +176,7 @@ struct carlb_env
         return s;
     }
     ArenaDev arena() const { return ArenaDev{ triV, triAng, cellStart, cellTris, hitWords, cellSph, carReach, cellV, ballGrid, ballDims[0], ballDims[1],
-                         ballDims[2], ballCellStart, ballCellTris, ballCellSph }; }
+                         ballDims[2], ballCellStart, ballCellTris, ballCellSph, hasNative, nativeV, nativeAng }; }
     Outputs outputs() const
     {
         return Outputs{ rewards, dones, scoreDiff, episodeTicks, tScoreDiff, tEpisodeTicks, overtime, tovertime };
@@ -418,7 +422,7 @@ carlb_status carlb_destroy(carlb_env* e);
 static carlb_status initEnv(carlb_env* p, const carlb_config* cfg)
 {
     std::string err;
-    const auto host = hostArena(arenaObjPath(libraryDir() + "/_data/arena.obj"), err);
+    const auto host = hostArena(arenaObjPath(libraryDir() + "/_data/arena.obj"), arenaMetadataPath(), err);
     if (!host) return fail(p, CARLB_ERR_STATE, err);
 
     p->cfg = *cfg;
@@ -577,6 +581,30 @@ static carlb_status initEnv(carlb_env* p, const carlb_config* cfg)
         ECHECK(p, cudaMemcpyAsync(p->ballCellSph, bsph.data(), bsph.size() * sizeof(float4), cudaMemcpyHostToDevice,
                                   p->stream));
         ECHECK(p, cudaStreamSynchronize(p->stream));  // the host vectors go out of scope
+    }
+    if (host->hasNative)
+    {
+        std::vector<float4> nv((size_t)nTris * 3), na(nTris);
+        for (int t = 0; t < nTris; t++)
+        {
+            for (int k = 0; k < 3; k++)
+            {
+                float w = 0.f;
+                if (k == 0) std::memcpy(&w, &host->nativeMesh[t], 4);
+                const float* v = &host->nativeVerts[9 * (size_t)t + 3 * k];
+                nv[3 * t + k] = make_float4(v[0], v[1], v[2], w);
+            }
+            float fw = 0.f;
+            std::memcpy(&fw, &host->nativeFlags[t], 4);
+            na[t] = make_float4(host->nativeAngles[3 * t], host->nativeAngles[3 * t + 1], host->nativeAngles[3 * t + 2], fw);
+        }
+        ECHECK(p, allocZero(p, &p->nativeV, nv.size()));
+        ECHECK(p, allocZero(p, &p->nativeAng, na.size()));
+        ECHECK(p, cudaMemcpyAsync(p->nativeV, nv.data(), nv.size() * sizeof(float4), cudaMemcpyHostToDevice, p->stream));
+        ECHECK(p, cudaMemcpyAsync(p->nativeAng, na.data(), na.size() * sizeof(float4), cudaMemcpyHostToDevice,
+                                  p->stream));
+        ECHECK(p, cudaStreamSynchronize(p->stream));
+        p->hasNative = 1;
     }
     ECHECK(p, allocZero(p, &p->cellSph, cellSph.size()));
     ECHECK(p, cudaMemcpyAsync(p->cellSph, cellSph.data(), cellSph.size() * sizeof(float4), cudaMemcpyHostToDevice,

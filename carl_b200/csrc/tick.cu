@@ -170,6 +170,134 @@ CB_D V3 loadBallScratch(const float* scratch, int stride, int s, int k)
     return V3{ scratch[(3 * k) * stride + s], scratch[(3 * k + 1) * stride + s], scratch[(3 * k + 2) * stride + s] };
 }
 
+// Native-metadata arena contacts of the ball (lane 0): entry `e` of the ball-cell
+// list (triangles in traversal-key order) is offered to the per-mesh reduction.
+// Returns false when the triangle makes no contact.
+__device__ bool nativeBallContact(const ArenaDev& arena, int tri, V3 centerBT, BallContact& c, int& mesh)
+{
+    const float4 p0 = __ldg(&arena.nativeV[3 * tri]), p1 = __ldg(&arena.nativeV[3 * tri + 1]);
+    const float4 p2 = __ldg(&arena.nativeV[3 * tri + 2]);
+    mesh = __float_as_int(p0.w);
+    if (mesh < 0) return false;
+    return nativeSphereTriangle(centerBT, V3{ p0.x, p0.y, p0.z }, V3{ p1.x, p1.y, p1.z }, V3{ p2.x, p2.y, p2.z }, c);
+}
+
+// Reduction state of the native branch: contacts are kept four per native mesh
+// (meshes arrive in traversal order, so each mesh's contacts are contiguous).
+struct NativeBallSet
+{
+    BallContact set[MAX_BALL_ARENA_CONTACTS];
+    int count = 0, mesh = -1, base = 0, local = 0;
+
+    __device__ void offer(const ArenaDev& arena, int tri, V3 center, V3 centerBT, BallContact c, int cmesh)
+    {
+        if (cmesh != mesh)
+        {
+            base = count;
+            local = 0;
+            mesh = cmesh;
+        }
+        int slot;
+        if (local < 4)
+        {
+            // Room for the four plane contacts stays reserved (more than 16
+            // contacting meshes would overflow the reference's own arrays).
+            if (count >= MAX_BALL_ARENA_CONTACTS - 4) return;
+            slot = local++;
+            count++;
+        }
+        else
+        {
+            slot = ballContactReplacement(set + base, c);
+        }
+        const float4 p0 = __ldg(&arena.nativeV[3 * tri]), p1 = __ldg(&arena.nativeV[3 * tri + 1]);
+        const float4 p2 = __ldg(&arena.nativeV[3 * tri + 2]);
+        const float4 ang = __ldg(&arena.nativeAng[tri]);
+        adjustNativeBallEdgeNormal(c, V3{ p0.x, p0.y, p0.z }, V3{ p1.x, p1.y, p1.z }, V3{ p2.x, p2.y, p2.z },
+                                   V3{ ang.x, ang.y, ang.z }, __float_as_int(ang.w));
+        c.point = centerBT + c.relPos + c.normal * c.depth;
+        c.tri = tri;
+        set[base + slot] = c;
+    }
+};
+
+// Arena contacts and solve of a moving ball with native mesh metadata, one warp:
+// the ball-cell list is tested across lanes, the per-mesh reduction in
+// traversal order and the solve run on lane 0, which returns the push velocity.
+__device__ V3 ballArenaSolveNative(const SmemSoa& cars, const SmemSoa& sims, int s, int nCars, int tick,
+                                   const ArenaDev& arena, int* wbuf, int lane, const BallPre& b, int start, int end)
+{
+    const V3 center = b.exportedPos;
+    const V3 centerBT = center * .02f;
+    int& hitCount = wbuf[WARP_HIT_BUF];
+    if (lane == 0) hitCount = 0;
+    __syncwarp();
+    for (int e = start + lane; e < end; e += 32)
+    {
+        BallContact c;
+        int mesh;
+        if (nativeBallContact(arena, __ldg(&arena.ballCellTris[e]), centerBT, c, mesh))
+        {
+            const int slot = atomicAdd(&hitCount, 1);
+            if (slot < WARP_HIT_BUF) wbuf[slot] = e;
+        }
+    }
+    __syncwarp();
+    V3 pushVel = v3zero();
+    if (lane == 0)
+    {
+        NativeBallSet ns;
+        const int n = hitCount;
+        if (n <= WARP_HIT_BUF)
+        {
+            // Entry order is traversal-key order.
+            for (int i = 1; i < n; i++)
+            {
+                const int v = wbuf[i];
+                int j = i - 1;
+                while (j >= 0 && wbuf[j] > v)
+                {
+                    wbuf[j + 1] = wbuf[j];
+                    j--;
+                }
+                wbuf[j + 1] = v;
+            }
+            for (int i = 0; i < n; i++)
+            {
+                const int tri = __ldg(&arena.ballCellTris[wbuf[i]]);
+                BallContact c;
+                int mesh;
+                nativeBallContact(arena, tri, centerBT, c, mesh);
+                ns.offer(arena, tri, center, centerBT, c, mesh);
+            }
+        }
+        else
+        {
+            for (int e = start; e < end; e++)
+            {
+                const int tri = __ldg(&arena.ballCellTris[e]);
+                BallContact c;
+                int mesh;
+                if (nativeBallContact(arena, tri, centerBT, c, mesh)) ns.offer(arena, tri, center, centerBT, c, mesh);
+            }
+        }
+        const int count = finishNativeBallContacts(ns.set, ns.count, center);
+        bool wasHit = false;
+        for (int k = 0; k < nCars; k++) wasHit |= ballHitPreviousTick(cars.n(C_BALL_HIT_TICK, s * nCars + k), tick);
+        BallBody body;
+        body.pos = center;
+        body.vel = b.preSolveBT * 50.f;
+        body.velNoExt = b.velNoExt;
+        body.ang = sims.v(S_BANG, s);
+        body.deltaVel = body.deltaAng = body.pushVel = body.pushAng = v3zero();
+        solveBallArenaN<MAX_BALL_ARENA_CONTACTS>(body, ns.set, count, wasHit);
+        sims.setv(S_BVEL, s, body.vel);
+        sims.setv(S_BANG, s, body.ang);
+        pushVel = body.pushVel;
+    }
+    return pushVel;
+}
+
 // Arena contacts and solve of a moving ball, executed by one warp: triangles of
 // the grid cells around the ball are tested across lanes, the order-dependent
 // contact reduction and solve run on lane 0, which returns the push velocity.
@@ -195,6 +323,7 @@ __device__ V3 ballArenaSolve(const SmemSoa& cars, const SmemSoa& sims, int s, in
         start = __ldg(&arena.ballCellStart[c]);
         end = __ldg(&arena.ballCellStart[c + 1]);
     }
+    if (arena.hasNative) return ballArenaSolveNative(cars, sims, s, nCars, tick, arena, wbuf, lane, b, start, end);
     int& hitCount = wbuf[WARP_HIT_BUF];
     if (lane == 0) hitCount = 0;
     __syncwarp();

@@ -28,6 +28,12 @@ struct ArenaDev
     const int* ballCellStart;
     const int* ballCellTris;
     const float4* ballCellSph;
+    // Native mesh metadata (ArenaHost::native*), used by the ball when hasNative:
+    // Bullet-unit vertices (w of vertex 0: the native mesh, negative = no ball
+    // contact), and the native edge angles with the edge flag bits in w.
+    int hasNative;
+    const float4* nativeV;    // [nTris * 3]
+    const float4* nativeAng;  // [nTris]
 };
 
 struct TickParams
