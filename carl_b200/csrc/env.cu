@@ -118,6 +118,9 @@ struct carlb_env
     bool fusedReset = true;
     // Obs / state rows written through per-warp staging tiles (CARLB_STAGED_PACK=0: a thread per row).
     bool stagedPack = true;
+    // An env step's packing and auto-reset in one kernel (CARLB_FUSED_EPILOGUE=1); the
+    // default runs the seven grid-wide kernels, which measured faster.
+    bool fusedEpilogue = false;
     int* tickDev = nullptr;
     struct TickGraph { int kind, nTicks; bool diag, timing; cudaGraphExec_t exec; };
     std::vector<TickGraph> graphs;
@@ -461,6 +464,7 @@ static carlb_status initEnv(carlb_env* p, const carlb_config* cfg)
     ECHECK(p, allocZero(p, &p->tEpisodeTicks, (size_t)cfg->n_sim));
     if (const char* fr = std::getenv("CARLB_FUSED_RESET")) p->fusedReset = std::atoi(fr) != 0;
     if (const char* sp = std::getenv("CARLB_STAGED_PACK")) p->stagedPack = std::atoi(sp) != 0;
+    if (const char* fe = std::getenv("CARLB_FUSED_EPILOGUE")) p->fusedEpilogue = std::atoi(fe) != 0;
     {
         const char* path = std::getenv("CARLB_TICK_PATH");
         p->staged = !(path && std::string(path) == "fused");
@@ -803,6 +807,15 @@ carlb_status carlb_env_step(carlb_env* e, carlb_action_kind kind, const void* ac
     if (s != CARLB_OK) return s;
     const GView g = e->view();
     const Outputs o = e->outputs();
+    if (e->fusedEpilogue)
+    {
+        const StepOutputs a{ e->obs, e->tobs, e->packed, e->tpacked, e->obsDim, e->stateDim, e->cfg.invert_orange,
+                             e->cfg.normalize, e->cfg.previous_controls, e->tick, e->cfg.frameskip, e->maxTicks,
+                             e->overtimeTicks, e->noTouchTicks };
+        launchStepEpilogue(g, o, a, e->stream);
+        ECHECK(e, cudaGetLastError());
+        return CARLB_OK;
+    }
     launchPackRewardsDones(g, o, e->tick, e->maxTicks, e->overtimeTicks, e->noTouchTicks, e->stream);
     launchPackState(g, e->tpacked, e->stateDim, e->tick, e->cfg.frameskip, nullptr, e->stream);
     launchPackObs(g, e->tobs, e->dones, e->obsDim, e->cfg.invert_orange, e->cfg.normalize, e->cfg.previous_controls, e->stream);

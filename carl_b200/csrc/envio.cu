@@ -117,10 +117,11 @@ __global__ void clearKernel(GView g)
 
 // ---- auto-reset after done ------------------------------------------------------------------------
 
-__global__ void resetDonesKernel(GView g, int tick, int maxTicks, int overtimeTicks, int noTouchTicks)
+// Auto-reset of one sim after its episode ended (src/RLEnvironment.cu:192-219,
+// State/Reset.cuh resetAfterDone): overtime starts on a tied regulation end,
+// otherwise a scored, timed-out or untouched episode restarts from a kickoff.
+__device__ void resetDoneSim(const GView& g, int sim, int tick, int maxTicks, int overtimeTicks, int noTouchTicks)
 {
-    const int sim = blockIdx.x * blockDim.x + threadIdx.x;
-    if (sim >= g.nSim) return;
     const GlobSoa& S = g.sim;
     const bool overtime = S.n(S_GOALS + G_OVERTIME, sim) != 0;
     const bool scored = S.n(S_GOALS + G_LAST_SCORER, sim) != 0;
@@ -165,6 +166,13 @@ __global__ void resetDonesKernel(GView g, int tick, int maxTicks, int overtimeTi
         }
     }
     for (int p = 0; p < NUM_BOOST_PADS; p++) S.f(S_PADS + p, sim) = 0.f;
+}
+
+__global__ void resetDonesKernel(GView g, int tick, int maxTicks, int overtimeTicks, int noTouchTicks)
+{
+    const int sim = blockIdx.x * blockDim.x + threadIdx.x;
+    if (sim >= g.nSim) return;
+    resetDoneSim(g, sim, tick, maxTicks, overtimeTicks, noTouchTicks);
 }
 
 // ---- observations -----------------------------------------------------------------------------------
@@ -449,24 +457,42 @@ __global__ void __launch_bounds__(PACK_THREADS) packStateWarpKernel(GView g, flo
     e.finish();
 }
 
-__global__ void packRewardsDonesKernel(GView g, Outputs out, int tick, int maxTicks, int overtimeTicks, int noTouchTicks)
+// Whether a sim's episode is over (Observations.cuh:360-397 packDones): a goal,
+// regulation time with a winner, expired overtime or the no-touch timeout.
+__device__ bool simDone(const GView& g, int sim, int tick, int maxTicks, int overtimeTicks, int noTouchTicks)
 {
-    const int sim = blockIdx.x * blockDim.x + threadIdx.x;
-    if (sim >= g.nSim) return;
     const GlobSoa& S = g.sim;
     const int blue = S.n(S_GOALS + G_BLUE, sim), orange = S.n(S_GOALS + G_ORANGE, sim);
     const int last = S.n(S_GOALS + G_LAST_SCORER, sim);
     const bool overtime = S.n(S_GOALS + G_OVERTIME, sim) != 0;
     const int ep = S.n(S_EP_TICKS, sim);
-    out.rewards[sim] = (float)last;
     const bool regulationExpired = ep >= maxTicks && blue != orange;
     const bool overtimeExpired = overtime && ep >= maxTicks + overtimeTicks;
     const bool gameOver = !overtime && regulationExpired;
     const bool timeout = noTouchTicks > 0 && tick - S.n(S_LAST_TOUCH, sim) >= noTouchTicks;
-    out.dones[sim] = (gameOver || overtimeExpired || timeout || last != 0) ? 1 : 0;
+    return gameOver || overtimeExpired || timeout || last != 0;
+}
+
+// Reward, done and transition match outputs of one sim (Observations.cuh:360-397).
+__device__ void packRewardsDonesSim(const GView& g, const Outputs& out, int sim, int tick, int maxTicks,
+                                    int overtimeTicks, int noTouchTicks)
+{
+    const GlobSoa& S = g.sim;
+    const int blue = S.n(S_GOALS + G_BLUE, sim), orange = S.n(S_GOALS + G_ORANGE, sim);
+    const bool overtime = S.n(S_GOALS + G_OVERTIME, sim) != 0;
+    const int ep = S.n(S_EP_TICKS, sim);
+    out.rewards[sim] = (float)S.n(S_GOALS + G_LAST_SCORER, sim);
+    out.dones[sim] = simDone(g, sim, tick, maxTicks, overtimeTicks, noTouchTicks) ? 1 : 0;
     out.transitionScoreDiff[sim] = blue - orange;
     out.transitionEpisodeTicks[sim] = ep;
     out.transitionOvertime[sim] = overtime ? 1 : 0;
+}
+
+__global__ void packRewardsDonesKernel(GView g, Outputs out, int tick, int maxTicks, int overtimeTicks, int noTouchTicks)
+{
+    const int sim = blockIdx.x * blockDim.x + threadIdx.x;
+    if (sim >= g.nSim) return;
+    packRewardsDonesSim(g, out, sim, tick, maxTicks, overtimeTicks, noTouchTicks);
 }
 
 __device__ void packRawMatchSim(const GView& g, const Outputs& out, int sim)
@@ -1113,6 +1139,97 @@ __global__ void __launch_bounds__(MASK_THREADS) actionMaskKernel(const float* ob
     }
 }
 
+// The env step's outputs after the ticks in one launch (python/carl.cu:312-370:
+// rewards and dones, transition state, transition obs of the done sims,
+// auto-reset, raw match state, obs, state).  A CTA owns EPI_AGENTS / nCars whole
+// sims: its agent warps hold a car each, its sim warps a sim each.  Every phase
+// only touches the CTA's own sims, so the per-sim order of the separate kernels
+// is kept with two CTA barriers:
+//   1. sim warps: rewards, dones, transition state rows; agent warps: transition
+//      obs rows of the done sims (each evaluates its sim's done flag itself);
+//   2. sim warps: auto-reset of the done sims;
+//   3. agent warps: obs rows; sim warps: raw match state and state rows.
+// Rows are written through the warps' staging tiles (a warp's agents, and its
+// sims, are consecutive rows).
+constexpr int EPI_AGENTS = 128;               // agent threads per CTA (4 warps)
+constexpr int EPI_MAX_WARPS = 8;              // 4 agent warps + up to 4 sim warps (one car per sim)
+
+__global__ void __launch_bounds__(EPI_MAX_WARPS * 32, 3) stepEpilogueKernel(GView g, Outputs o, StepOutputs a)
+{
+    extern __shared__ float tileMem[];  // [warps][32][33]
+    float(*tile)[32][33] = reinterpret_cast<float(*)[32][33]>(tileMem);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int simsPerCta = EPI_AGENTS / g.nCars;
+    const int sim0 = blockIdx.x * simsPerCta;
+    const int nS = min(simsPerCta, g.nSim - sim0);
+    const int agents = nS * g.nCars;
+    const long long agent0 = (long long)sim0 * g.nCars;
+    const bool agentWarp = tid < EPI_AGENTS;
+    // Agent role: agent index inside the CTA; sim role: sim index inside the CTA.
+    const int idx = agentWarp ? tid : tid - EPI_AGENTS;
+    const bool live = agentWarp ? idx < agents : idx < nS;
+    const int first = agentWarp ? (warp * 32) : (warp - EPI_AGENTS / 32) * 32;  // index of lane 0
+    const bool warpLive = first < (agentWarp ? agents : nS);
+    int sim, local = 0;
+    if (agentWarp)
+    {
+        const long long ag = agent0 + min(idx, agents - 1);
+        sim = (int)(ag / g.nCars);
+        local = (int)(ag - (long long)sim * g.nCars);
+    }
+    else
+    {
+        sim = sim0 + min(idx, nS - 1);
+    }
+
+    if (!agentWarp)
+    {
+        if (live) packRewardsDonesSim(g, o, sim, a.tick, a.maxTicks, a.overtimeTicks, a.noTouchTicks);
+        if (warpLive)
+        {
+            WarpRows e{ tile[warp], a.tstate + (long long)(sim0 + first) * a.stateDim, a.stateDim, lane, 0,
+                        __ballot_sync(0xffffffffu, live), false };
+            emitStateRow(g, e, a.tick, a.frameskip, sim);
+            e.finish();
+        }
+    }
+    else if (warpLive)
+    {
+        const bool done = live && simDone(g, sim, a.tick, a.maxTicks, a.overtimeTicks, a.noTouchTicks);
+        const unsigned rows = __ballot_sync(0xffffffffu, done);
+        if (rows)
+        {
+            WarpRows e{ tile[warp], a.tobs + (agent0 + first) * a.obsDim, a.obsDim, lane, 0, rows, a.normalize != 0 };
+            emitObsRow(g, e, a.invertOrange, a.previousControls, sim, local);
+            e.finish();
+        }
+    }
+    __syncthreads();
+    if (!agentWarp && live) resetDoneSim(g, sim, a.tick, a.maxTicks, a.overtimeTicks, a.noTouchTicks);
+    __syncthreads();
+    if (agentWarp)
+    {
+        if (warpLive)
+        {
+            WarpRows e{ tile[warp], a.obs + (agent0 + first) * a.obsDim, a.obsDim, lane, 0,
+                        __ballot_sync(0xffffffffu, live), a.normalize != 0 };
+            emitObsRow(g, e, a.invertOrange, a.previousControls, sim, local);
+            e.finish();
+        }
+    }
+    else
+    {
+        if (live) packRawMatchSim(g, o, sim);
+        if (warpLive)
+        {
+            WarpRows e{ tile[warp], a.state + (long long)(sim0 + first) * a.stateDim, a.stateDim, lane, 0,
+                        __ballot_sync(0xffffffffu, live), false };
+            emitStateRow(g, e, a.tick, 1, sim);
+            e.finish();
+        }
+    }
+}
+
 inline int blocks(long long n, int t) { return (int)((n + t - 1) / t); }
 
 }  // namespace
@@ -1181,6 +1298,14 @@ void launchActionMask(const float* obs, long long rows, int obsDim, bool previou
         actionMaskKernel<<<blocks(rows, MASK_THREADS), MASK_THREADS, 0, s>>>(obs, rows, obsDim,
                                                                             previousControls ? OBS_PREVIOUS_CONTROLS : 0,
                                                                             mask);
+}
+void launchStepEpilogue(const GView& g, const Outputs& o, const StepOutputs& a, cudaStream_t s)
+{
+    if (g.nSim <= 0) return;
+    const int simsPerCta = EPI_AGENTS / g.nCars;
+    const int threads = EPI_AGENTS + 32 * ((simsPerCta + 31) / 32);
+    const size_t smem = (size_t)(threads / 32) * 32 * 33 * sizeof(float);
+    stepEpilogueKernel<<<blocks(g.nSim, simsPerCta), threads, smem, s>>>(g, o, a);
 }
 void launchResetMasked(const GView& g, const ArenaDev& a, const BallInputs& ball, const CarInputs& cars,
                        const MatchInputs& match, const uint8_t* mask, const PackTargets& pk, cudaStream_t s)

@@ -62,6 +62,14 @@ struct PackTargets
     Outputs outputs;
 };
 
+// Output buffers and limits of an env step's epilogue.
+struct StepOutputs
+{
+    float *obs, *tobs, *state, *tstate;
+    int obsDim, stateDim, invertOrange, normalize, previousControls;
+    int tick, frameskip, maxTicks, overtimeTicks, noTouchTicks;
+};
+
 int uploadEnvioTables(const Tables& t);
 void launchClear(const GView& g, cudaStream_t s);
 void launchKickoff(const GView& g, int tick, cudaStream_t s);
@@ -79,6 +87,9 @@ void launchSetCar(const GView& g, const ArenaDev& a, const CarInputs& in, int n,
 void launchSetMatch(const GView& g, const int32_t* blue, const int32_t* orange, const int32_t* ticks, int n,
                     const int64_t* idx, const uint8_t* mask, cudaStream_t s);
 void launchResetPads(const GView& g, int n, const int64_t* idx, const uint8_t* mask, cudaStream_t s);
+// Everything an env step does after its ticks, in one launch: rewards / dones,
+// transition state and obs (done sims), auto-reset, raw match, obs and state.
+void launchStepEpilogue(const GView& g, const Outputs& o, const StepOutputs& a, cudaStream_t s);
 // Action mask rows [rows, ACTION_LOGITS] (u8) of observation rows [rows, obsDim].
 void launchActionMask(const float* obs, long long rows, int obsDim, bool previousControls, uint8_t* mask,
                       cudaStream_t s);
