@@ -185,8 +185,10 @@ def world_groups(args) -> int:
 
 
 def launches_per_step(groups: int) -> int:
-    """Kernels of the library launched per step: 8 stage kernels per tick and slice."""
-    return 8 * TICKS_PER_STEP * groups
+    """Kernels of the library launched per step: 8 stage kernels per tick and slice,
+    plus, with graph replay (the default), the kernel that sets the tick counter."""
+    graph = os.environ.get("CARLB_GRAPH", "1") != "0"
+    return 8 * TICKS_PER_STEP * groups + (1 if graph else 0)
 
 
 def measured_hbm_peak() -> tuple[float, str]:
