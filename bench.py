@@ -191,6 +191,19 @@ def launches_per_step(groups: int) -> int:
     return 8 * TICKS_PER_STEP * groups + (1 if graph else 0)
 
 
+def fp32_flops_per_car_tick() -> float | None:
+    """FP32 FLOPs per car per tick summed over the stage kernels, from the
+    committed ncu summary (sass thread fadd/fmul/ffma counts)."""
+    import re
+
+    try:
+        text = (ROOT / "profiles" / "staged_tick_3v3_32768.md").read_text()
+    except OSError:
+        return None
+    vals = [float(m.group(1)) for m in re.finditer(r"fp32_flops_per_car_tick\[\w+\]: (\d+(?:\.\d+)?)", text)]
+    return sum(vals) if vals else None
+
+
 def measured_hbm_peak() -> tuple[float, str]:
     try:
         peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
@@ -409,6 +422,17 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     roofline_tick = {"bound": "hbm", "achieved": tick_achieved, "peak": peak, "unit": "GB/s",
                      "frac": tick_achieved / peak, "model": "CARLB-v1", "bytes_per_agent_tick": bpat,
                      "tick_ms": tick_ms}
+    # FP32 SIMT roof of the whole tick: counted FLOPs per car-tick (ncu summary)
+    # over the nominal FP32 peak at the sampled maximum SM clock.
+    flops = fp32_flops_per_car_tick()
+    roofline_fp32 = None
+    if flops:
+        sm_max = float(clocks.get("sm_max_mhz") or 1965.0)
+        fp32_peak = 148 * 128 * 2 * sm_max * 1e6 / 1e12
+        fp32_achieved = flops * n_total_cars / (tick_ms / 1e3) / 1e12
+        roofline_fp32 = {"bound": "fp32", "achieved": fp32_achieved, "peak": fp32_peak, "unit": "TFLOP/s",
+                         "frac": fp32_achieved / fp32_peak, "flop_per_car_tick": flops,
+                         "peak_kind": "nominal: 148 SMs x 128 FP32 lanes x 2 FLOP x max SM clock"}
     if staged:
         # A stage kernel launch covers one sim slice (the timed one is slice 0).
         groups = world_groups(args)
@@ -453,7 +477,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
                    "wall_s": wall},
         "clocks": clocks, "e2e": e2e,
         "gpu_launches": args.steps * (launches_per_step(world_groups(args)) if staged else 1),
-        "roofline": roofline, "roofline_tick": roofline_tick, "cpu_baseline": cpu,
+        "roofline": roofline, "roofline_tick": roofline_tick, "roofline_fp32": roofline_fp32, "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)
     env.close()
