@@ -608,6 +608,15 @@ extern "C" int hosttick_ball_grid(void* h, float* geom, int* dims)
     return 0;
 }
 
+// Loads native mesh metadata into the env's arena tables (carl_b200/csrc/arena.cpp
+// loadNativeMetadata): 0, or 1 with the error in hosttick_error().
+extern "C" int hosttick_load_metadata(void* h, const char* path)
+{
+    auto* e = static_cast<HostEnv*>(h);
+    g_error = loadNativeMetadata(path, e->arena);
+    return g_error.empty() ? 0 : 1;
+}
+
 extern "C" int hosttick_ball_lists(void* h, int* start, int* tris)
 {
     auto* e = static_cast<HostEnv*>(h);

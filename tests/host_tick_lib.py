@@ -50,6 +50,7 @@ def _load():
         lib.hosttick_kickoff_table.argtypes = [ctypes.c_void_p] * 2
         lib.hosttick_ball_grid.argtypes = [ctypes.c_void_p] * 3
         lib.hosttick_ball_lists.argtypes = [ctypes.c_void_p] * 3
+        lib.hosttick_load_metadata.argtypes = [ctypes.c_void_p, ctypes.c_char_p]
         _lib = lib
     return _lib
 
@@ -109,6 +110,11 @@ class HostTick:
                                                  ("verts", "tris", "prefix", "tri_idx", "edge_angles", "normals",
                                                   "flags")])
         return out
+
+    def load_metadata(self, path) -> None:
+        """Native mesh metadata into the product's arena tables (raises with its error)."""
+        if self.lib.hosttick_load_metadata(self.h, str(path).encode()) != 0:
+            raise RuntimeError(self.lib.hosttick_error().decode())
 
     def ball_grid(self):
         """(origin[3], cell size, dims[3], cell starts, cell triangle lists) of the product's ball grid."""

@@ -87,6 +87,22 @@ def test_null_handles_fail_cleanly(lib):
     assert lib.carlb_create(None, None) == capi.ERR_VALUE
 
 
+def test_action_mask_validates_before_launch(lib):
+    """carlb_action_mask checks its arguments before any device work (no GPU needed)."""
+    err = lambda: lib.carlb_last_error(None).decode()  # noqa: E731
+    assert lib.carlb_action_mask(None, 0, 200, 0, None, None) == capi.OK  # nothing to do
+    assert lib.carlb_action_mask(None, -1, 200, 0, None, None) == capi.ERR_VALUE
+    assert "non-negative" in err()
+    assert lib.carlb_action_mask(None, 4, 200, 0, None, None) == capi.ERR_VALUE
+    assert "null" in err()
+    assert lib.carlb_action_mask(16, 4, 200, 0, 18, None) == capi.ERR_VALUE
+    assert "aligned" in err()
+    assert lib.carlb_action_mask(16, 4, 36, 0, 16, None) == capi.ERR_VALUE
+    assert "obs_dim" in err()
+    # With previous controls the ego fields sit 8 values further from the end.
+    assert lib.carlb_action_mask(16, 4, 44, 1, 16, None) == capi.ERR_VALUE
+
+
 def test_create_without_a_device_reports_cuda_error(lib):
     import torch
 
