@@ -65,6 +65,9 @@ def test_step_returns_obs_view(env):
     obs = env.step(actions)
     assert obs.shape == (8, 2, env.obs_dim) and obs.dtype == torch.float32 and obs.is_cuda
     assert obs.data_ptr() == env.get_obs().data_ptr()  # the same in-place buffer
+    # DLPack export as the reference's capsules: a CUDA device tuple, zero copy.
+    assert obs.__dlpack_device__() == (2, torch.cuda.current_device())
+    assert torch.from_dlpack(obs).data_ptr() == obs.data_ptr()
     assert env.get_dones().dtype == torch.bool and env.get_rewards().shape == (8,)
     assert env.get_state().shape == (8, 9 + 2 * 22 + 34)
     assert torch.isfinite(obs).all()
