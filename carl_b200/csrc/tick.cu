@@ -1810,8 +1810,12 @@ int launchTick(const TickParams& p, const ArenaDev& a, void* stream)
 
 
 // ---- fixed-size scratch for carlb_ticks_static_scratch --------------------------------------
-// A file-scope device array, so that entry point allocates nothing at call time.
-// Calls that overlap in time (any env, any stream) share it and race.
+// A file-scope device array, so that entry point allocates nothing at call time
+// (for callers that cannot call cudaMalloc while stepping).  Every GPU that loads
+// the library holds it until the process exits.  Host code must not use its name
+// as an address (on the host it is only a stand-in): staticScratchAddress looks
+// the device address up.  Calls that overlap on the GPU (any env, any stream)
+// share it and race.
 static __device__ __align__(256) unsigned char g_staticScratch[STATIC_SCRATCH_BYTES];
 
 int staticScratchAddress(void** ptr, size_t* bytes)

@@ -225,14 +225,21 @@ carlb_status carlb_ticks(carlb_env* env, carlb_action_kind kind, const void* act
  * may be NULL) happen on the env stream; returns after the stream drains. */
 carlb_status carlb_ticks_host(carlb_env* env, carlb_action_kind kind, const void* host_actions,
                               int32_t n_ticks, float* host_rewards);
-/* Same ticks as carlb_ticks, with the stage scratch taken from a fixed-size
- * file-scope device array (64 MiB) instead of the env's own scratch, so the call
- * allocates nothing (no cudaMalloc/cudaFree, no allocating library call).  The
- * array's address is looked up once per device.  Returns CARLB_ERR_VALUE when the
- * env needs more scratch than the array holds, CARLB_ERR_STATE on the fused path.
- * The array is shared: calls that overlap in time (any env, any stream) race, so
- * serialise them.  The first call on a device does the one-time lookup, so make
- * it before capturing any stream.  No counterpart in the reference. */
+/* Same ticks as carlb_ticks, for callers that must not allocate device memory
+ * while they step: a control loop with a latency budget, where cudaMalloc and
+ * cudaFree can stall on the whole device, or a process whose device memory is
+ * owned by another allocator (a framework's caching pool), where a new
+ * cudaMalloc can fail.  This call allocates nothing (no cudaMalloc, cudaFree or
+ * allocating library routine): the stage scratch comes from a fixed 64 MiB
+ * file-scope device array, which every GPU that loads this library holds until
+ * the process exits.  Its address is looked up on the first call on each
+ * device, so make that first call before capturing any stream.  An env that
+ * needs more than 64 MiB of stage scratch (roughly 224 bytes per car and 64 per
+ * sim: about 47,000 sims at 3v3) gets CARLB_ERR_VALUE; the fused tick path gets
+ * CARLB_ERR_STATE.  Every call shares the array, which keeps the last call's
+ * contents (the work-list counters are cleared on each call), so calls that
+ * overlap on the GPU (any env, any stream) race: serialise them.  No counterpart
+ * in the reference. */
 carlb_status carlb_ticks_static_scratch(carlb_env* env, carlb_action_kind kind, const void* actions,
                                         int32_t n_ticks);
 carlb_status carlb_reset(carlb_env* env);

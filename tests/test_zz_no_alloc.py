@@ -1,7 +1,11 @@
-"""carlb_ticks_static_scratch: the staged ticks with the stage scratch taken
-from a fixed-size file-scope device array (no allocation at call time) give
-the same state as carlb_ticks, over two consecutive calls, and an env that
-needs more scratch than the array holds is rejected."""
+"""carlb_ticks_static_scratch, the tick entry point for callers that must not
+allocate device memory while they step (a latency-bound control loop, where
+cudaMalloc can stall the device, or a process whose device memory belongs to
+another allocator, where it can fail).  Its stage scratch is a fixed 64 MiB
+file-scope device array.  Two calls in a row give the same state as
+carlb_ticks, and an env that needs more scratch than the array holds is
+rejected.  This file is collected last, so a run that stops at the first
+failure has run every other test before it."""
 
 from __future__ import annotations
 
