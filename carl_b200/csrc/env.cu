@@ -122,7 +122,14 @@ struct carlb_env
     // default runs the seven grid-wide kernels, which measured faster.
     bool fusedEpilogue = false;
     int* tickDev = nullptr;
-    struct TickGraph { int kind, nTicks; bool diag, timing; cudaGraphExec_t exec; };
+    // Host actions of carlb_ticks_host copied slice by slice on their own stream, each
+    // slice's controls stage waiting for its rows (CARLB_OVERLAP_COPY=0: one copy on the
+    // env stream before the launch).  Created on first use.
+    bool overlapCopy = true;
+    cudaStream_t copyStream = nullptr;
+    cudaEvent_t actionsIn = nullptr;
+    cudaEvent_t actionsReady[8] = {};
+    struct TickGraph { int kind, nTicks; bool diag, timing, hostIn; cudaGraphExec_t exec; };
     std::vector<TickGraph> graphs;
 
     float *obs = nullptr, *tobs = nullptr, *packed = nullptr, *tpacked = nullptr, *rewards = nullptr;
@@ -158,9 +165,10 @@ struct carlb_env
         g.simOffset = cfg.sim_offset;
         return g;
     }
-    StageStreams stageStreams() const
+    StageStreams stageStreams(bool hostIn = false) const
     {
         StageStreams s{};
+        for (int g = 0; g < 8; g++) s.actionsReady[g] = hostIn ? actionsReady[g] : nullptr;
         s.groups = groups;
         for (int g = 0; g < 8; g++)
         {
@@ -232,7 +240,9 @@ int chooseTileSims(int nCars, int hitWords)
 
 size_t actionRowBytes(carlb_action_kind kind) { return kind == CARLB_ACTIONS_DIRECT ? 32 : 28; }
 
-carlb_status launchTicks(carlb_env* e, carlb_action_kind kind, int nTicks)
+// hostIn: the actions are being copied in per slice on the copy stream
+// (stageHostActionsSliced), so each slice's controls stage waits for its rows.
+carlb_status launchTicks(carlb_env* e, carlb_action_kind kind, int nTicks, bool hostIn = false)
 {
     TickParams p{};
     p.car = e->car;
@@ -260,7 +270,8 @@ carlb_status launchTicks(carlb_env* e, carlb_action_kind kind, int nTicks)
     {
         cudaGraphExec_t exec = nullptr;
         for (const auto& g : e->graphs)
-            if (g.kind == (int)kind && g.nTicks == nTicks && g.diag == e->diagnostics && g.timing == e->stageTiming)
+            if (g.kind == (int)kind && g.nTicks == nTicks && g.diag == e->diagnostics && g.timing == e->stageTiming &&
+                g.hostIn == hostIn)
                 exec = g.exec;
         if (!exec && e->graphs.size() < 16)
         {
@@ -270,7 +281,7 @@ carlb_status launchTicks(carlb_env* e, carlb_action_kind kind, int nTicks)
             TickParams q = p;
             q.tickDev = e->tickDev;
             ECHECK(e, cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
-            const int lerr = launchTickStaged(q, e->arena(), e->scratch, e->stream, e->stageStreams());
+            const int lerr = launchTickStaged(q, e->arena(), e->scratch, e->stream, e->stageStreams(hostIn));
             cudaGraph_t graph = nullptr;
             const cudaError_t cerr = cudaStreamEndCapture(e->stream, &graph);
             if (lerr || cerr != cudaSuccess)
@@ -281,7 +292,7 @@ carlb_status launchTicks(carlb_env* e, carlb_action_kind kind, int nTicks)
             const cudaError_t ierr = cudaGraphInstantiate(&exec, graph, 0);
             cudaGraphDestroy(graph);
             if (ierr != cudaSuccess) return cudaFail(e, ierr, "tick graph instantiate");
-            e->graphs.push_back({ (int)kind, nTicks, e->diagnostics, e->stageTiming, exec });
+            e->graphs.push_back({ (int)kind, nTicks, e->diagnostics, e->stageTiming, hostIn, exec });
         }
         if (exec)
         {
@@ -297,7 +308,7 @@ carlb_status launchTicks(carlb_env* e, carlb_action_kind kind, int nTicks)
     }
     ECHECK(e, cudaEventRecord(e->ev0, e->stream));
     const int err = e->staged
-        ? launchTickStaged(p, e->arena(), e->scratch, e->stream, e->stageStreams())
+        ? launchTickStaged(p, e->arena(), e->scratch, e->stream, e->stageStreams(hostIn))
         : launchTick(p, e->arena(), e->stream);
     if (err) return cudaFail(e, (cudaError_t)err, "tick kernel launch");
     e->stageTimed = e->staged && e->stageTiming && nTicks > 0;
@@ -313,6 +324,51 @@ carlb_status stageActions(carlb_env* e, carlb_action_kind kind, const void* src,
     if (!src) return fail(e, CARLB_ERR_VALUE, "actions pointer is null");
     const size_t bytes = (size_t)e->nCarTotal * actionRowBytes(kind);
     ECHECK(e, cudaMemcpyAsync(e->actions, src, bytes, dir, e->stream));
+    return CARLB_OK;
+}
+
+// Number of non-empty sim slices of a staged launch.
+int sliceCount(const carlb_env* e)
+{
+    int n = 0;
+    for (int g = 0; g < 8; g++)
+    {
+        int s0 = 0, ns = 0;
+        stageSlice(e->cfg.n_sim, e->groups, g, &s0, &ns);
+        if (ns <= 0) break;
+        n++;
+    }
+    return n;
+}
+
+// Host actions for a staged launch, copied slice by slice on the copy stream after
+// the work already queued on the env stream (which covers the last launch's reads of
+// the action buffer); actionsReady[g] marks slice g's rows.  The caller launches with
+// hostIn, so each slice's controls stage waits for its own rows only.
+carlb_status stageHostActionsSliced(carlb_env* e, carlb_action_kind kind, const void* src)
+{
+    if (kind != CARLB_ACTIONS_DISCRETE && kind != CARLB_ACTIONS_CONTINUOUS && kind != CARLB_ACTIONS_DIRECT)
+        return fail(e, CARLB_ERR_VALUE, "unknown action kind");
+    if (!src) return fail(e, CARLB_ERR_VALUE, "actions pointer is null");
+    if (!e->copyStream)
+    {
+        ECHECK(e, cudaStreamCreateWithFlags(&e->copyStream, cudaStreamNonBlocking));
+        ECHECK(e, cudaEventCreateWithFlags(&e->actionsIn, cudaEventDisableTiming));
+        for (int g = 0; g < 8; g++) ECHECK(e, cudaEventCreateWithFlags(&e->actionsReady[g], cudaEventDisableTiming));
+    }
+    ECHECK(e, cudaEventRecord(e->actionsIn, e->stream));
+    ECHECK(e, cudaStreamWaitEvent(e->copyStream, e->actionsIn, 0));
+    const size_t rowBytes = (size_t)e->nCars * actionRowBytes(kind);
+    for (int g = 0; g < 8; g++)
+    {
+        int s0 = 0, ns = 0;
+        stageSlice(e->cfg.n_sim, e->groups, g, &s0, &ns);
+        if (ns <= 0) break;
+        ECHECK(e, cudaMemcpyAsync(static_cast<char*>(e->actions) + (size_t)s0 * rowBytes,
+                                  static_cast<const char*>(src) + (size_t)s0 * rowBytes, (size_t)ns * rowBytes,
+                                  cudaMemcpyHostToDevice, e->copyStream));
+        ECHECK(e, cudaEventRecord(e->actionsReady[g], e->copyStream));
+    }
     return CARLB_OK;
 }
 
@@ -477,6 +533,7 @@ static carlb_status initEnv(carlb_env* p, const carlb_config* cfg)
         if (const char* b = std::getenv("CARLB_BALL_STREAM")) p->ballSide = std::atoi(b) != 0;
         if (const char* o = std::getenv("CARLB_PHASE_OFFSET")) p->phaseOffset = std::atoi(o) != 0;
         if (const char* gr = std::getenv("CARLB_GRAPH")) p->useGraph = std::atoi(gr) != 0;
+        if (const char* oc = std::getenv("CARLB_OVERLAP_COPY")) p->overlapCopy = std::atoi(oc) != 0;
         if (p->useGraph) ECHECK(p, allocZero(p, &p->tickDev, (size_t)1));
         for (int g = 0; g < p->groups; g++)
         {
@@ -682,6 +739,14 @@ carlb_status carlb_destroy(carlb_env* e)
         if (e->ballStream[g]) cudaStreamDestroy(e->ballStream[g]);
     }
     if (e->evFork) cudaEventDestroy(e->evFork);
+    if (e->copyStream)
+    {
+        cudaStreamSynchronize(e->copyStream);
+        cudaStreamDestroy(e->copyStream);
+    }
+    if (e->actionsIn) cudaEventDestroy(e->actionsIn);
+    for (int g = 0; g < 8; g++)
+        if (e->actionsReady[g]) cudaEventDestroy(e->actionsReady[g]);
     for (int k = 0; k < 2 * STAGE_KERNELS; k++)
         if (e->stageEv[k]) cudaEventDestroy(e->stageEv[k]);
     if (e->stream) cudaStreamDestroy(e->stream);
@@ -784,10 +849,17 @@ carlb_status carlb_ticks_host(carlb_env* e, carlb_action_kind kind, const void* 
 {
     if (!e) return fail(nullptr, CARLB_ERR_VALUE, "env is null");
     if (n < 0) return fail(e, CARLB_ERR_VALUE, "n_ticks must be non-negative");
-    carlb_status s = stageActions(e, kind, hostActions, cudaMemcpyHostToDevice);
+    cudaStreamCaptureStatus outer = cudaStreamCaptureStatusNone;
+    ECHECK(e, cudaStreamIsCapturing(e->stream, &outer));
+    const bool sliced = e->staged && e->overlapCopy && n > 0 && outer == cudaStreamCaptureStatusNone;
+    carlb_status s = sliced ? stageHostActionsSliced(e, kind, hostActions)
+                            : stageActions(e, kind, hostActions, cudaMemcpyHostToDevice);
     if (s != CARLB_OK) return s;
-    s = launchTicks(e, kind, n);
+    s = launchTicks(e, kind, n, sliced);
     if (s != CARLB_OK) return s;
+    // The slices' controls stages already waited for their rows; this orders the
+    // env stream after the last copy as well, whatever the launch read.
+    if (sliced) ECHECK(e, cudaStreamWaitEvent(e->stream, e->actionsReady[sliceCount(e) - 1], 0));
     if (hostRewards)
     {
         launchPackRewardsDones(e->view(), e->outputs(), e->tick, e->maxTicks, e->overtimeTicks, e->noTouchTicks, e->stream);

@@ -1899,11 +1899,10 @@ int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch&
     StageScratch gx[STAGE_MAX_GROUPS];
     cudaStream_t gs[STAGE_MAX_GROUPS];
     int nG = 0;
-    const int per = (p.nSim + groups - 1) / groups;
     for (int g = 0; g < groups; g++)
     {
-        const int s0 = g * per;
-        const int ns = std::min(per, p.nSim - s0);
+        int s0 = 0, ns = 0;
+        stageSlice(p.nSim, groups, g, &s0, &ns);
         if (ns <= 0) break;
         const long long c0 = (long long)s0 * p.nCars;
         TickParams q = p;
@@ -1989,6 +1988,18 @@ int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch&
             mark(1, false, sq);
             flatKernel<<<(n + CAND_BLOCK - 1) / CAND_BLOCK, CAND_BLOCK, candSmem, sq>>>(q, a, y, t);
             mark(1, true, sq);
+            // Actions copied in per slice beside the launch: the controls stage is the
+            // first reader (the finish after it the only other), so the copy overlaps
+            // the first tick's broadphase.
+            if (t == 0 && aux.actionsReady[g])
+            {
+                cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+                cudaStreamIsCapturing(sq, &cs);
+                if ((err = cudaStreamWaitEvent(sq, (cudaEvent_t)aux.actionsReady[g],
+                                               cs == cudaStreamCaptureStatusActive ? cudaEventWaitExternal
+                                                                                   : cudaEventWaitDefault)) != cudaSuccess)
+                    return (int)err;
+            }
             mark(2, false, sq);
             rayCtlKernel<<<(n + RAY_BLOCK - 1) / RAY_BLOCK, RAY_BLOCK, 0, sq>>>(q, a, y, t);
             mark(2, true, sq);

@@ -106,7 +106,19 @@ struct StageStreams
     void* wideDone[8];    // optional event per slice: its wide stages of the tick (phase offset)
     void* stageEvents[2 * STAGE_KERNELS];  // optional: start / end events of slice 0's stage
                                            // kernels in the last tick of the launch
+    void* actionsReady[8];  // optional event per slice: its action rows are in place (recorded on
+                            // a copy stream before the launch; the slice's first controls stage waits)
 };
+
+// Sims [*s0, *s0 + *ns) of slice g when nSim sims are stepped as `groups` slices
+// (clamped to 1..8); *ns <= 0 means slice g is empty.
+inline void stageSlice(int nSim, int groups, int g, int* s0, int* ns)
+{
+    groups = groups < 1 ? 1 : (groups > 8 ? 8 : groups);
+    const int per = (nSim + groups - 1) / groups;
+    *s0 = g * per;
+    *ns = nSim - *s0 < per ? nSim - *s0 : per;
+}
 
 // Capacity of the file-scope device scratch used by carlb_ticks_static_scratch.
 constexpr size_t STATIC_SCRATCH_BYTES = 64ull << 20;

@@ -222,7 +222,11 @@ carlb_status carlb_env_step(carlb_env* env, carlb_action_kind kind, const void* 
 carlb_status carlb_ticks(carlb_env* env, carlb_action_kind kind, const void* actions, int32_t n_ticks);
 /* Same as carlb_ticks but `host_actions` is host memory: the copy to the device,
  * the ticks and a copy back of the packed rewards into `host_rewards` (f32 [n_sim],
- * may be NULL) happen on the env stream; returns after the stream drains. */
+ * may be NULL) are ordered after the work already on the env stream; returns after
+ * the stream drains, so both buffers are free again on return.  On the staged path
+ * the actions are copied slice by slice on a side stream and each sim slice starts
+ * its controls stage once its own rows are in (the copy overlaps the first tick's
+ * broadphase; pinned host memory lets it run asynchronously). */
 carlb_status carlb_ticks_host(carlb_env* env, carlb_action_kind kind, const void* host_actions,
                               int32_t n_ticks, float* host_rewards);
 /* Same ticks as carlb_ticks, for callers that must not allocate device memory
