@@ -1657,13 +1657,16 @@ __global__ void __launch_bounds__(CC_BLOCK) carCarKernel(TickParams p, int t)
             for (int q = 0; q < nPairs && q < DIAG_SIM_WORDS; q++) p.diagSim[q * p.simStride + s] = 0;
     }
     __syncthreads();
+    // The active sims are packed into the first lanes; those lanes of each warp
+    // step their sims together.
+    const unsigned lanes = __ballot_sync(FULL, tid < nActive);
     if (tid >= nActive) return;
     const int sIdx = activeS[tid];
     const int sb = sIdx * nCars;
     SimCars<CarSoa> sc{ cars, sb, nCars, p.nBlue, (int)(p.globalCarBase + sb), tick, p.seed };
     int kept[DIAG_SIM_WORDS];
     const bool diag = lastTick && p.diagSim;
-    solveCarCarSim(sc, kept, diag ? DIAG_SIM_WORDS : 0);
+    solveCarCarSim(sc, kept, diag ? DIAG_SIM_WORDS : 0, lanes);
     if (diag)
         for (int q = 0; q < nPairs && q < DIAG_SIM_WORDS; q++) p.diagSim[q * p.simStride + sIdx] = kept[q];
 }
