@@ -88,6 +88,9 @@ def parse_args():
                     help="c3: the headline tick throughput; step: env steps at frameskip 8 (ticks + packing); "
                          "reset: env steps with masked resets (C5 shard); mask: device action masks")
     ap.add_argument("--reset-n-sim", type=int, default=131072, help="sims of the reset workload (4v4)")
+    ap.add_argument("--frameskip", type=int, default=TICKS_PER_STEP,
+                    help="ticks per env step of the step workload (1 with --blue 1 --orange 1 --n-sim 65536: "
+                         "config C2, obs packed every tick)")
     return ap.parse_args()
 
 
@@ -515,7 +518,9 @@ def run_env_workload(args, resets: bool) -> None:
     own CUDA build (`carlrefgpu_time_reset_steps`).
 
     step:  config C3 (3v3, n_sim sims, seeded floor states), frameskip 8 (the
-           gymnasium wrapper's default), discrete actions; env-steps/s.
+           gymnasium wrapper's default), discrete actions; env-steps/s.  Team
+           sizes, sims and frameskip follow --blue/--orange/--n-sim/--frameskip
+           (C2: 1v1, 65536 sims, frameskip 1, so obs are packed every tick).
     reset: config C5's per-GPU shard (4v4, --reset-n-sim sims, C4 mixed states),
            frameskip 1, each env step followed by a masked apply_reset_state
            that puts a random 1 % of the sims back to their kickoff state; the
@@ -530,7 +535,7 @@ def run_env_workload(args, resets: bool) -> None:
         n_sim, frameskip = args.reset_n_sim, 1
     else:
         nb, no = args.blue, args.orange
-        n_sim, frameskip = args.n_sim, TICKS_PER_STEP
+        n_sim, frameskip = args.n_sim, args.frameskip
     n_cars = nb + no
     rng = np.random.default_rng(args.seed + 5)
     rows = kickoff_rows(n_sim, nb, no, args.seed) if resets else None
@@ -601,8 +606,9 @@ def run_env_workload(args, resets: bool) -> None:
         data = "synthetic (seeded C4 mixed states, discrete actions, random 1% masks, kickoff reset rows)"
     else:
         metric = f"env-steps/sec at {nb}v{no} n_sim={n_sim}, frameskip {frameskip}"
-        workload = f"C3 {nb}v{no} n_sim={n_sim}, env_step (frameskip {frameskip} ticks + packing), discrete actions"
-        data = "synthetic (seeded C3 floor states, discrete actions)"
+        name = "C2" if (nb, no, frameskip) == (1, 1, 1) else "C3"
+        workload = f"{name} {nb}v{no} n_sim={n_sim}, env_step (frameskip {frameskip} ticks + packing), discrete actions"
+        data = "synthetic (seeded floor states, discrete actions)"
     line = {
         "metric": metric, "value": ours["agent_steps_per_s"] if resets else ours["env_steps_per_s"],
         "unit": UNIT if resets else "env-steps/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
