@@ -624,6 +624,44 @@ static carlb_status initEnv(carlb_env* p, const carlb_config* cfg)
     std::vector<float4> cellV(3 * host->cellTris.size());
     for (size_t e = 0; e < host->cellTris.size(); e++)
         for (int k = 0; k < 3; k++) cellV[3 * e + k] = triV[3 * (size_t)host->cellTris[e] + k];
+    // Margin of the flat stage's plane pre-test per triangle, in distance units
+    // times |n| (n = cross(v1 - v0, v2 - v0), the unnormalised normal the test
+    // uses).  A box centre that passed the reach cull lies within D = 2r + carReach
+    // of every vertex (r: the bounding-sphere radius).  The car-frame SAT projects
+    // vertices at most D away onto a normal built from edges at least Lmin long,
+    // so its rounding is bounded by a few ulp of D plus the normal's direction
+    // error times D, about 1e-7 * D * D / Lmin.  The margin takes 100 times those
+    // terms, plus 0.05 uu.  Degenerate triangles get an infinite margin (no skip).
+    {
+        std::vector<float> marginN(nTris);
+        for (int t = 0; t < nTris; t++)
+        {
+            double v[3][3];
+            for (int k = 0; k < 3; k++)
+                for (int d = 0; d < 3; d++) v[k][d] = (double)host->verts[3 * host->tris[3 * t + k] + d];
+            double e1[3], e2[3], e3[3];
+            for (int d = 0; d < 3; d++)
+            {
+                e1[d] = v[1][d] - v[0][d];
+                e2[d] = v[2][d] - v[0][d];
+                e3[d] = v[2][d] - v[1][d];
+            }
+            const double n[3] = { e1[1] * e2[2] - e1[2] * e2[1], e1[2] * e2[0] - e1[0] * e2[2],
+                                  e1[0] * e2[1] - e1[1] * e2[0] };
+            const double nl = std::sqrt(n[0] * n[0] + n[1] * n[1] + n[2] * n[2]);
+            auto len = [](const double* a) { return std::sqrt(a[0] * a[0] + a[1] * a[1] + a[2] * a[2]); };
+            const double lmin = std::min(len(e1), std::min(len(e2), len(e3)));
+            const double D = 2.0 * (double)triSph[t].w + (double)p->carReach;
+            if (nl < 1e-3 || lmin < 1e-3)
+            {
+                marginN[t] = INFINITY;
+                continue;
+            }
+            const double margin = 0.05 + 1e-4 * D + 1e-5 * D * D / lmin;
+            marginN[t] = (float)(margin * nl * (1.0 + 1e-6));
+        }
+        for (size_t e = 0; e < host->cellTris.size(); e++) cellV[3 * e + 1].w = marginN[host->cellTris[e]];
+    }
     ECHECK(p, allocZero(p, &p->cellV, cellV.size()));
     ECHECK(p, cudaMemcpyAsync(p->cellV, cellV.data(), cellV.size() * sizeof(float4), cudaMemcpyHostToDevice,
                               p->stream));

@@ -1208,8 +1208,20 @@ __global__ void __launch_bounds__(CAND_BLOCK) flatKernel(TickParams p, ArenaDev 
         {
             const V3 cc = { poseS[0 * B + c], poseS[1 * B + c], poseS[2 * B + c] };
             const Q4 cr = { poseS[3 * B + c], poseS[4 * B + c], poseS[5 * B + c], poseS[6 * B + c] };
-            const LocalTri lt = localTriangle(cc, cr, v0, v1, v2);
-            if (carTriSat(lt).overlap) atomicOr(&hitS[(k >> 5) * B + c], 1u << (k & 31));
+            // Plane pre-test in world space: a box whose centre is farther from the
+            // triangle's plane than the box reaches along the normal, by more than the
+            // entry's margin (q1.w, scaled by |n|; it bounds the rounding of this test
+            // and of the car-frame one), is separated on the triangle-normal axis,
+            // where the car-frame SAT would report no overlap too.  Only the other
+            // triangles go through the exact SAT.
+            const V3 nw = cross(e1, e2);
+            const float off = dot(nw, cc - v0);
+            const float ext = dot(vabs(unrotate(cr, nw)), carHalfExtents());
+            if (!(fabsf(off) > ext + q1.w))
+            {
+                const LocalTri lt = localTriangle(cc, cr, v0, v1, v2);
+                if (carTriSat(lt).overlap) atomicOr(&hitS[(k >> 5) * B + c], 1u << (k & 31));
+            }
         }
     };
     for (int itA = tid; itA < total; itA += 2 * B)

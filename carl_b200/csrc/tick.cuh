@@ -20,7 +20,8 @@ struct ArenaDev
     const float4* cellSph;  // [cellStart[NUM_CELLS]]: bounding sphere of cellTris[e] (centre xyz, radius w),
                             // radius rounded up
     float carReach;         // radius around a car's box centre that holds its box and wheel rays, plus margin
-    const float4* cellV;    // [3 * cellStart[NUM_CELLS]]: vertices of cellTris[e] (flags in vertex 0's w)
+    const float4* cellV;    // [3 * cellStart[NUM_CELLS]]: vertices of cellTris[e] (flags in vertex 0's w;
+                            // vertex 1's w: the plane pre-test margin times |cross(v1 - v0, v2 - v0)|)
     // Ball grid (ArenaHost::ball*): origin xyz and 1 / cell size in w, dimensions,
     // per-cell triangle lists and the bounding sphere of each list entry.
     float4 ballGrid;
