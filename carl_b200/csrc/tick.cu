@@ -1512,7 +1512,11 @@ __device__ __forceinline__ Body loadHeavyBody(const CarSoa& cars, const StageScr
 }
 
 // Manifold solve and final store of a listed car (src/Physics/CarArena/Solve.cuh order).
-__device__ __forceinline__ void finishContactCar(const CarSoa& cars, int i, Body& body, MPoint* pts, int cnt)
+// Not inlined: the contact kernel's plane-only and mesh paths share one copy of
+// the manifold solve, which keeps the kernel's code and registers smaller.  The
+// floor workloads gain (3v3 bench step 2.56-2.58 against 2.60 ms, 1v1 floor 1.71
+// against 1.76), the contact-heavy 2v2 mixed loses 2 % (3.63 against 3.55 ms).
+__device__ __noinline__ void finishContactCar(const CarSoa& cars, int i, Body& body, MPoint* pts, int cnt)
 {
     if (cnt > 0)
     {
