@@ -1,28 +1,43 @@
 """Throughput benchmark of the batched Rocket League tick on B200.
 
-Workload (config C3): 3v3, n_sim = 32768 sims per GPU, default arena, seeded
-synthetic initial states (cars uniform over the field floor, planar velocity
-N(0, 800 uu/s), yaw uniform, boost U[0, 100], ball at rest at centre) and
-direct controls redrawn every 8 ticks (throttle/steer/pitch/yaw/roll U[-1, 1],
-jump/boost/handbrake Bernoulli(0.3)).
+Default workload (config C3): 3v3, n_sim = 32768 sims per GPU, default arena,
+seeded synthetic initial states (cars uniform over the field floor, planar
+velocity N(0, 800 uu/s), yaw uniform, boost U[0, 100], ball at rest at centre)
+and direct controls redrawn every 8 ticks (throttle/steer/pitch/yaw/roll
+U[-1, 1], jump/boost/handbrake Bernoulli(0.3)).  The tick runs in the default
+mode (compat_flags = 0), which reproduces the reference's CUDA build and is the
+mode the parity tests hold to the strict gates.
 
-A *step* is one control period: the controls for all cars are staged and 8
-physics ticks run (one launch of the fused tick kernel).  The metric is
-agent-steps/s = cars x ticks / s, one agent-step being one car advanced one
-120 Hz tick.
+A *step* is one control period: the controls for all cars are staged on the
+device and 8 physics ticks run (one replay of the captured stage-kernel graph).
+The metric is agent-steps/s = cars x ticks / s, one agent-step being one car
+advanced one 120 Hz tick.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                  [--workload c3|c1|c4|c5|step|mask]
+
+  c1    1v1, n_sim = 1024 per GPU, kickoff resets (the launch-overhead regime)
+  c4    2v2, 262,144 sims over 8 GPUs (32,768 per GPU), 50 % airborne, 25 % on
+        walls / ceiling, 25 % near corners and goal mouths
+  c5    4v4, 1,048,576 sims over 8 GPUs (131,072 per GPU), the C4 states, env
+        steps at frameskip 1 with 1 % of sims reset to kickoff by a masked
+        apply_reset_state each step and the obs handed to torch each step
+  step  env steps (ticks + packing) at frameskip 8 (C2 with --blue 1 --orange 1
+        --n-sim 65536 --frameskip 1)
+  mask  device action masks of a C5 shard's observations
 
 For N > 1 it runs under torch.distributed.run, one rank per GPU; each rank
 simulates its own contiguous slice of sims (global sim offset rank*n_sim), so
 per-GPU work is fixed (weak scaling) and there is no collective in the tick.
 
-Timed region: barrier + synchronize, K steps, synchronize + barrier.  Each
-step's device time is taken with CUDA events on the env stream; between timed
-steps a 256 MiB buffer is written to flush the 126 MB L2 (outside the events).
-The roofline uses the event-timed duration of the dominant stage kernel (CUDA
-events around each stage kernel of the first sim slice, last tick of each step),
-and a second figure covers the whole tick.
+Timed region: barrier + synchronize, K steps enqueued back to back (no host
+synchronisation between them), synchronize + barrier.  Each step's device time
+is taken with CUDA events on the env stream; before each timed step a 256 MiB
+buffer is written on the same stream (outside the events) to flush the 126 MB
+L2.  The value uses the maximum over ranks of the summed step times.  Stage
+kernel times, work-list sizes and the per-stage rooflines come from a separate
+pass after the timed region (events around each stage kernel of the first sim
+slice, last tick of each step).
 """
 
 from __future__ import annotations
@@ -49,23 +64,52 @@ FLUSH_BYTES = 256 << 20
 # actions read.
 BYTES_PER_CAR_TICK = 620
 BYTES_PER_SIM_TICK = 504
-# Algorithmic bytes of single stage kernels, per car and per sim of one tick:
-# the words the stage must read and write (arena tables are L2-resident and
-# excluded).  flat: pose in (pos, vel, ang, cen, rot: 16 words), candidate
-# list start, count, SAT hit mask (9 words) and ray keys (8 words) out, episode
-# tick read-modify-write per sim.  rayCtl: pose, keys, controls state in
-# (74 words), rays, wheel bits and controls state out (62 words), ball position
-# per sim.  susp: hits, rays, body, suspension, friction and manifold state in
-# (70 words), suspension state, friction and velocities out (33 words).
-# ballPrep: ball state in (22 words), hand-over values out (15 words).
+# Algorithmic bytes of each stage kernel: the words the stage must read and
+# write per car and per sim of its slice, and per entry of the work lists it
+# runs over (arena tables are L2-resident and excluded).
+#   flat      pose in (pos, vel, ang, cen, rot: 16 words), candidate list start,
+#             count, SAT hit mask (9 words) and ray keys (8 words) out, episode
+#             tick read-modify-write per sim.
+#   rayCtl    pose, keys, controls state in (74 words), rays, wheel bits and
+#             controls state out (62 words), ball position per sim.
+#   susp      hits, rays, body, suspension, friction and manifold state in
+#             (70 words), suspension state, friction and velocities out
+#             (33 words).
+#   contact   per listed car: hand-over velocities (18 words), pose, candidate
+#             range and hit mask in (20 words), pose, velocities and manifold
+#             count and normal out (20 words).
+#   carCar    the pair gate of every sim: box centre and demolition flag of
+#             each car (4 words); per sim with a pair in reach: every car's
+#             pose, velocities, impulse and contact state in and out (2 x 24
+#             words per car).
+#   ball      per moving ball: ball state and hand-over values in (27 words),
+#             velocities and push velocity out (9 words).
+#   finish    per car: pose, velocities, impulse, demolition and respawn state,
+#             boost and controls in (34 words), pose, velocities, impulse and
+#             finish state out (22 words); per sim: ball state and hand-over
+#             values in (40 words) and out (26 words), 34 pad cooldowns and the
+#             goal state in and out (78 words).
+#   ballPrep  ball state in (22 words), hand-over values out (15 words).
 STAGE_BYTES = {
-    "flat": (140, 8),
-    "rayCtl": (544, 12),
-    "susp": (412, 0),
-    "ballPrep": (0, 148),
+    # stage: (bytes per car, bytes per sim, {work list: bytes per entry})
+    "ballPrep": (0, 148, {}),
+    "flat": (140, 8, {}),
+    "rayCtl": (544, 12, {}),
+    "susp": (412, 0, {}),
+    "contact": (0, 0, {"plane_cars": 232, "sat_cars": 232}),
+    "carCar": (16, 0, {"car_car_sims_cars": 192}),
+    "ball": (0, 0, {"moving_balls": 144}),
+    "finish": (224, 576, {}),
 }
-METRIC = "agent-steps/sec at 3v3 n_sim=32768"
 UNIT = "agent-steps/s"
+
+
+def metric_name(args) -> str:
+    if args.workload == "c1":
+        return "agent-steps/sec at 1v1 n_sim=1024 (C1)"
+    if args.workload == "c4":
+        return "agent-steps/sec at 2v2 n_sim=32768 per GPU (C4)"
+    return f"agent-steps/sec at {args.blue}v{args.orange} n_sim={args.n_sim}"
 
 
 def bytes_per_agent_tick(n_cars: int) -> float:
@@ -84,32 +128,43 @@ def parse_args():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--workload", choices=["c3", "step", "reset", "mask"], default="c3",
-                    help="c3: the headline tick throughput; step: env steps at frameskip 8 (ticks + packing); "
-                         "reset: env steps with masked resets (C5 shard); mask: device action masks")
-    ap.add_argument("--reset-n-sim", type=int, default=131072, help="sims of the reset workload (4v4)")
+    ap.add_argument("--no-stages", action="store_true", help="skip the stage-timing pass")
+    ap.add_argument("--workload", choices=["c3", "c1", "c4", "c5", "reset", "step", "mask"], default="c3",
+                    help="c3: the headline tick throughput; c1 / c4: the other tick configs; c5 (alias reset): env "
+                         "steps with masked resets and obs handed to torch; step: env steps at frameskip 8; "
+                         "mask: device action masks")
+    ap.add_argument("--reset-n-sim", type=int, default=131072, help="sims per GPU of the c5 workload (4v4)")
     ap.add_argument("--frameskip", type=int, default=TICKS_PER_STEP,
                     help="ticks per env step of the step workload (1 with --blue 1 --orange 1 --n-sim 65536: "
                          "config C2, obs packed every tick)")
-    return ap.parse_args()
+    args = ap.parse_args()
+    if args.workload == "reset":
+        args.workload = "c5"
+    if args.workload == "c1":
+        args.blue, args.orange, args.n_sim = 1, 1, 1024
+    elif args.workload == "c4":
+        args.blue, args.orange, args.n_sim = 2, 2, 32768
+    return args
 
 
 # ---------------------------------------------------------------- clocks ----
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed
+    region, for the GPUs of this run (one sampler per node, on local rank 0)."""
 
     QUERY = ("index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
     REASONS = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
-    def __init__(self, device: int):
-        self.bus_id = ""
+    def __init__(self, devices: list[int]):
+        self.bus_ids = set()
         try:
             import torch
 
-            pr = torch.cuda.get_device_properties(device)
-            self.bus_id = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            for d in devices:
+                pr = torch.cuda.get_device_properties(d)
+                self.bus_ids.add(f"{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0")
         except Exception:
             pass
         self.proc = None
@@ -136,7 +191,8 @@ class ClockSampler:
             f = [x.strip() for x in line.split(",")]
             if len(f) < 10:
                 continue
-            if self.bus_id and f[1].lower()[-12:] != self.bus_id[-12:]:
+            # nvidia-smi prints domain:bus:device.function; compare bus:device.function.
+            if self.bus_ids and f[1].lower()[-7:] not in self.bus_ids:
                 continue
             rows.append(f)
         os.unlink(self.path)
@@ -146,16 +202,42 @@ class ClockSampler:
         mx = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
         reasons = sorted({name for r in rows for name, v in zip(self.REASONS, r[6:10]) if v.lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "gpus": len(self.bus_ids)}
 
 
 # ------------------------------------------------------------ workload ----
+def initial_state(args, env, seed: int) -> None:
+    """The workload's seeded initial state (C3 floor, C1 kickoff, C4 mixed)."""
+    from carl_b200 import workloads
+
+    if args.workload == "c1":
+        env.reset()
+    elif args.workload == "c4":
+        workloads.mixed_state(env, seed)
+    else:
+        workloads.floor_state(env, seed)
+
+
+def workload_name(args) -> str:
+    if args.workload == "c1":
+        return "C1 1v1 n_sim=1024 per GPU, kickoff reset, direct controls held 8 ticks"
+    if args.workload == "c4":
+        return ("C4 2v2 n_sim=32768 per GPU (262,144 over 8 GPUs), 50% airborne / 25% walls and ceiling / "
+                "25% corners and goal mouths, direct controls held 8 ticks")
+    return f"C3 {args.blue}v{args.orange} n_sim={args.n_sim} per GPU, direct controls held 8 ticks"
+
+
+def data_name(args) -> str:
+    states = {"c1": "kickoff states", "c4": "C4 mixed states"}.get(args.workload, "C3 floor states")
+    return f"synthetic (seeded {states}, direct controls redrawn every 8 ticks)"
+
+
 def make_env(args, rank: int, device: int):
-    from carl_b200 import capi, workloads
+    from carl_b200 import capi
 
     env = capi.Env(args.n_sim, args.blue, args.orange, seed=args.seed, device=device,
                    sim_offset=rank * args.n_sim)
-    workloads.floor_state(env, args.seed + 1000 * rank)
+    initial_state(args, env, args.seed + 1000 * rank)
     return env
 
 
@@ -167,16 +249,14 @@ def control_pool(n_cars_total: int, count: int, seed: int):
 
 
 def traffic_per_launch(stage: str, n_sim: int) -> float | None:
-    """DRAM bytes per launch of a stage kernel, from the committed ncu summary
-    of the staged tick (stated for n_sim = 32768, 2 slices; traffic grows with
-    the sims, so it is scaled to this run's n_sim).  None when not captured."""
-    path = ROOT / "profiles" / "staged_tick_3v3_32768.md"
-    if not path.exists():
-        return None
+    """DRAM bytes per launch of a stage kernel, from the committed ncu summaries
+    (stated for a slice of the n_sim = 32768 bench; traffic grows with the sims,
+    so it is scaled to this run's n_sim).  None when not captured."""
     key = f"traffic_bytes_per_launch[{stage}]:"
-    for line in path.read_text().splitlines():
-        if line.startswith(key):
-            return float(line.split(":", 1)[1].split()[0]) * n_sim / 32768
+    for path in sorted((ROOT / "profiles").glob("*.md")):
+        for line in path.read_text().splitlines():
+            if line.startswith(key):
+                return float(line.split(":", 1)[1].split()[0]) * n_sim / 32768
     return None
 
 
@@ -215,6 +295,19 @@ def measured_hbm_peak() -> tuple[float, str]:
         return 6650.0, "fallback"
 
 
+def stage_bytes(stage: str, cars: float, sims: float, work: dict) -> float:
+    """Algorithmic bytes of one launch of `stage` over `cars` cars and `sims`
+    sims, with the work-list sizes `work` of the same slice."""
+    per_car, per_sim, per_entry = STAGE_BYTES[stage]
+    total = per_car * cars + per_sim * sims
+    for name, b in per_entry.items():
+        if name == "car_car_sims_cars":
+            total += b * work.get("car_car_sims", 0) * (cars / max(sims, 1))
+        else:
+            total += b * work.get(name, 0)
+    return total
+
+
 # -------------------------------------------------------- reference CPU ----
 def reference_cpu_time(snapshot, n_sim, n_blue, n_orange, seed, controls, steps, threads):
     """Times the reference's tick compiled for the host (OpenMP over sims).
@@ -243,37 +336,36 @@ def host_threads() -> int:
 
 # ------------------------------------------------------------- arms --------
 def run_reference(args, rank: int, world: int) -> None:
-    """The reference arm: the reference's own CPU tick on the host cores."""
+    """The reference arm: the reference's own CPU tick on the host cores, plus
+    its CUDA build on the same states and controls when a GPU is present."""
     if rank != 0:
         return
-    from carl_b200 import capi, workloads
-
-    n_cars = args.blue + args.orange
-    # The initial state is built on the host restatement of the reference so the
-    # arm needs no GPU: kickoff reset, then the same seeded floor distribution.
     from oracle.refenv import RefCpu
 
+    n_cars = args.blue + args.orange
+    # The initial state is built on the host build of the reference so the arm
+    # needs no GPU for its headline value.
     threads = host_threads()
     RefCpu.set_threads(threads)
     ref = RefCpu(args.n_sim, args.blue, args.orange, args.seed)
-    workloads.floor_state(ref, args.seed)
+    initial_state(args, ref, args.seed)
     snap = ref.snapshot()
     ref.close()
     pool_n = max(4, min(16, args.steps + args.warmup))
     ctl = control_pool(args.n_sim * n_cars, pool_n, args.seed + 1)
-    steps = max(1, min(args.steps, 8))
+    steps = max(1, min(args.steps, 8 if args.n_sim * n_cars > 50000 else 200))
     warm = max(0, min(args.warmup, 1))
     if warm:
         reference_cpu_time(snap, args.n_sim, args.blue, args.orange, args.seed, ctl, warm, threads)
     value, secs, used = reference_cpu_time(snap, args.n_sim, args.blue, args.orange, args.seed, ctl, steps, threads)
-    sample = (f"{steps} steps x {TICKS_PER_STEP} ticks of the full 3v3 n_sim={args.n_sim} workload "
-              f"({secs:.1f} s), OpenMP over sims")
+    sample = (f"{steps} steps x {TICKS_PER_STEP} ticks of the full {args.blue}v{args.orange} n_sim={args.n_sim} "
+              f"workload ({secs:.1f} s), OpenMP over sims")
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps,
-        "warmup": warm, "ms_per_step": secs * 1e3 / steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded C3 floor states, direct controls)",
-        "config": {"workload": f"C3 {args.blue}v{args.orange} n_sim={args.n_sim}, direct controls held 8 ticks",
-                   "ticks_per_step": TICKS_PER_STEP, "implementation": "reference tick compiled for the host CPU"},
+        "impl": "reference", "metric": metric_name(args), "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": steps, "warmup": warm, "ms_per_step": secs * 1e3 / steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": data_name(args),
+        "config": {"workload": workload_name(args), "ticks_per_step": TICKS_PER_STEP,
+                   "implementation": "reference tick compiled for the host CPU"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": used, "kind": "reference", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "cuda_build": reference_cuda_time(args, snap, ctl),
@@ -306,6 +398,23 @@ def reference_cuda_time(args, snapshot, controls) -> dict | None:
     return {"value": args.n_sim * n_cars * TICKS_PER_STEP * args.steps / (total / 1e3), "unit": UNIT,
             "ms_per_step": total / args.steps, "steps": args.steps, "warmup": args.warmup,
             "what": "reference CUDA build (its sources, nvcc sm_100a --fmad=false -rdc), same states and controls"}
+
+
+def stage_pass(env, step, first: int, count: int) -> tuple[dict, dict]:
+    """Untimed pass with stage timing on: mean stage kernel ms (first sim slice,
+    last tick of each step) and mean work-list sizes (all slices)."""
+    env.set_stage_timing(True)
+    times: dict[str, list[float]] = {}
+    work: dict[str, list[int]] = {}
+    for i in range(count):
+        step(first + i)
+        env.synchronize()
+        for k, v in env.stage_times().items():
+            times.setdefault(k, []).append(v)
+        for k, v in env.stage_work().items():
+            work.setdefault(k, []).append(v)
+    env.set_stage_timing(False)
+    return ({k: sum(v) / len(v) for k, v in times.items()}, {k: sum(v) / len(v) for k, v in work.items()})
 
 
 def run_b200(args, rank: int, world: int, local_rank: int) -> None:
@@ -342,46 +451,52 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         step(i)
     env.synchronize()
 
-    # ---- timed region ----
+    # ---- timed region: K steps enqueued back to back ----
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    kernel_ms = []
-    stage_ms: dict[str, list[float]] = {}
-    try:
-        env.set_stage_timing(True)
-        staged = True
-    except capi.CarlbError:  # the fused path (CARLB_TICK_PATH=fused) has one kernel per launch
-        staged = False
-    sampler = ClockSampler(device)
-    sampler.start()
+    enqueue_s = []
+    sampler = ClockSampler(list(range(world))) if local_rank == 0 else None
+    if sampler:
+        sampler.start()
     barrier()
     torch.cuda.synchronize()
     wall0 = time.perf_counter()
     for i in range(args.steps):
         with torch.cuda.stream(stream):
             flush.fill_(i & 0xFF)
-            starts[i].record(stream)
+        h0 = time.perf_counter()
+        starts[i].record(stream)
         step(args.warmup + i)
         ends[i].record(stream)
-        env.synchronize()
-        kernel_ms.append(env.last_tick_ms())
-        if staged:
-            for name, ms in env.stage_times().items():
-                stage_ms.setdefault(name, []).append(ms)
+        enqueue_s.append(time.perf_counter() - h0)
     torch.cuda.synchronize()
-    barrier()
     wall = time.perf_counter() - wall0
-    clocks = sampler.stop()
-    step_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
-    kern_ms = sum(kernel_ms)
+    barrier()
+    clocks = sampler.stop() if sampler else None
+    step_times = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    step_ms_rank = sum(step_times)
+    ms_mine = env.last_tick_ms()  # device span of the last step's tick kernels
 
-    t = torch.tensor([step_ms, kern_ms], dtype=torch.float64, device=dev)
+    # ---- stage times and work lists (untimed pass) ----
+    stage_avg, work_avg = ({}, {}) if args.no_stages else stage_pass(env, step, args.warmup + args.steps,
+                                                                         min(10, max(3, args.steps // 4)))
+
+    # ---- per-rank record, gathered on every rank (same collective order everywhere) ----
+    stage_names = list(capi.Env.STAGES)
+    rec = [step_ms_rank, wall, 1e3 * statistics.mean(enqueue_s), 1e3 * max(enqueue_s), max(step_times),
+           min(step_times), ms_mine] + [stage_avg.get(k, 0.0) for k in stage_names]
+    t = torch.tensor(rec, dtype=torch.float64, device=dev)
     if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    step_ms, kern_ms = float(t[0]), float(t[1])
-    if staged:
-        env.set_stage_timing(False)
-    stage_avg = {k: sum(v) / len(v) for k, v in stage_ms.items()}
+        gathered = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(gathered, t)
+        rows = [g.tolist() for g in gathered]
+    else:
+        rows = [t.tolist()]
+    step_ms = max(r[0] for r in rows)
+    per_rank = [{"rank": r, "ms_per_step": row[0] / args.steps, "wall_s": row[1], "enqueue_ms_mean": row[2],
+                 "enqueue_ms_max": row[3], "step_ms_max": row[4], "step_ms_min": row[5],
+                 "stage_ms": {k: round(v, 4) for k, v in zip(stage_names, row[7:]) if v}}
+                for r, row in enumerate(rows)]
 
     agent_ticks_rank = n_total_cars * TICKS_PER_STEP * args.steps
     value = agent_ticks_rank * world / (step_ms / 1e3)
@@ -417,42 +532,42 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         env.close()
         return
 
-    # ---- roofline of the dominant stage kernel, and of the whole tick ----
+    # ---- rooflines: whole tick from the event-timed step, and every stage kernel ----
     peak, peak_kind = measured_hbm_peak()
     bpat = bytes_per_agent_tick(n_cars)
-    tick_ms = kern_ms / args.steps / TICKS_PER_STEP
+    tick_ms = step_ms / args.steps / TICKS_PER_STEP
     tick_achieved = bpat * n_total_cars / (tick_ms / 1e3) / 1e9
     roofline_tick = {"bound": "hbm", "achieved": tick_achieved, "peak": peak, "unit": "GB/s",
                      "frac": tick_achieved / peak, "model": "CARLB-v1", "bytes_per_agent_tick": bpat,
-                     "tick_ms": tick_ms}
-    # FP32 SIMT roof of the whole tick: counted FLOPs per car-tick (ncu summary)
-    # over the nominal FP32 peak at the sampled maximum SM clock.
+                     "tick_ms": tick_ms, "tick_ms_source": "event-timed step (max over ranks) / 8"}
     flops = fp32_flops_per_car_tick()
     roofline_fp32 = None
     if flops:
-        sm_max = float(clocks.get("sm_max_mhz") or 1965.0)
+        sm_max = float((clocks or {}).get("sm_max_mhz") or 1965.0)
         fp32_peak = 148 * 128 * 2 * sm_max * 1e6 / 1e12
         fp32_achieved = flops * n_total_cars / (tick_ms / 1e3) / 1e12
         roofline_fp32 = {"bound": "fp32", "achieved": fp32_achieved, "peak": fp32_peak, "unit": "TFLOP/s",
                          "frac": fp32_achieved / fp32_peak, "flop_per_car_tick": flops,
                          "peak_kind": "nominal: 148 SMs x 128 FP32 lanes x 2 FLOP x max SM clock"}
-    if staged:
-        # A stage kernel launch covers one sim slice (the timed one is slice 0).
+    roofline = None
+    if stage_avg:
+        # A stage kernel launch covers one sim slice (the timed one is slice 0);
+        # work lists are summed over slices, so one slice gets its share.
         groups = world_groups(args)
-        modelled = {k: v for k, v in stage_avg.items() if k in STAGE_BYTES}
-        dom = max(modelled, key=modelled.get)
-        per_car, per_sim = STAGE_BYTES[dom]
-        dom_bytes = (per_car * n_total_cars + per_sim * args.n_sim) / groups
-        dom_ms = stage_avg[dom]
-        achieved = dom_bytes / (dom_ms / 1e3) / 1e9
-        roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+        slice_cars, slice_sims = n_total_cars / groups, args.n_sim / groups
+        slice_work = {k: v / groups for k, v in work_avg.items()}
+        per_stage = {}
+        for k, ms in stage_avg.items():
+            b = stage_bytes(k, slice_cars, slice_sims, slice_work)
+            per_stage[k] = {"ms": round(ms, 4), "algorithmic_bytes": b,
+                            "achieved_gbs": round(b / (ms / 1e3) / 1e9, 2), "frac": b / (ms / 1e3) / 1e9 / peak}
+        dom = max(stage_avg, key=stage_avg.get)
+        d = per_stage[dom]
+        roofline = {"bound": "hbm", "achieved": d["achieved_gbs"], "peak": peak, "unit": "GB/s", "frac": d["frac"],
                     "traffic": traffic_per_launch(dom, args.n_sim), "peak_kind": peak_kind, "kernel": dom + "Kernel",
-                    "launch_ms": dom_ms, "algorithmic_bytes_per_launch": dom_bytes, "sim_slices": groups,
-                    "stage_ms": {k: round(v, 4) for k, v in stage_avg.items()},
-                    "largest_stage": max(stage_avg, key=stage_avg.get)}
-    else:
-        roofline = dict(roofline_tick, kernel="tickKernel (fused, 8 ticks per launch)", peak_kind=peak_kind,
-                        traffic=None, launch_ms=kern_ms / args.steps)
+                    "launch_ms": d["ms"], "algorithmic_bytes_per_launch": d["algorithmic_bytes"],
+                    "sim_slices": groups, "selection": "the stage kernel with the longest mean duration",
+                    "stages": per_stage, "work_lists_per_tick": {k: round(v, 1) for k, v in work_avg.items()}}
 
     cpu = None
     if snap0 is not None:
@@ -466,21 +581,22 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
                                                    threads)
             steps_done = more
         cpu = {"value": v, "unit": UNIT, "cores": used, "kind": "reference",
-               "sample": f"{steps_done} steps x {TICKS_PER_STEP} ticks of the same 3v3 n_sim={args.n_sim} workload "
-                         f"({secs_tot:.1f} s) with the reference tick compiled for the host, OpenMP over sims"}
+               "sample": f"{steps_done} steps x {TICKS_PER_STEP} ticks of the same {args.blue}v{args.orange} "
+                         f"n_sim={args.n_sim} workload ({secs_tot:.1f} s) with the reference tick compiled for the "
+                         f"host, OpenMP over sims"}
 
     line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "metric": metric_name(args), "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": step_ms / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded C3 floor states, direct controls redrawn every 8 ticks)",
-        "config": {"workload": f"C3 {args.blue}v{args.orange} n_sim={args.n_sim} per GPU, direct controls held 8 ticks",
-                   "ticks_per_step": TICKS_PER_STEP, "sims_total": args.n_sim * world,
-                   "parallelism": f"sim-sharded x{world}", "l2": "256 MiB buffer written between timed steps",
-                   "wall_s": wall},
+        "vs_baseline": None, "dtype": "f32", "data": data_name(args),
+        "config": {"workload": workload_name(args), "ticks_per_step": TICKS_PER_STEP,
+                   "sims_total": args.n_sim * world, "parallelism": f"sim-sharded x{world}",
+                   "compat_flags": 0, "semantics": "the reference's CUDA build (default mode)",
+                   "l2": "256 MiB buffer written before each timed step", "wall_s": wall},
         "clocks": clocks, "e2e": e2e,
-        "gpu_launches": args.steps * (launches_per_step(world_groups(args)) if staged else 1),
+        "gpu_launches": args.steps * launches_per_step(world_groups(args)),
         "roofline": roofline, "roofline_tick": roofline_tick, "roofline_fp32": roofline_fp32, "cpu_baseline": cpu,
+        "per_rank": per_rank,
     }
     print(json.dumps(line), flush=True)
     env.close()
@@ -511,25 +627,46 @@ def kickoff_rows(n_sim: int, nb: int, no: int, seed: int) -> dict:
     return {k: np.ascontiguousarray(v) for k, v in rows.items()}
 
 
-def run_env_workload(args, resets: bool) -> None:
+class _ArrayInterface:
+    """A float32 device buffer of the env described for torch.as_tensor."""
+
+    def __init__(self, ptr: int, shape: tuple):
+        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": tuple(shape), "typestr": "<f4",
+                                         "strides": None, "version": 3, "stream": None}
+
+
+def device_view(env, which: int, torch):
+    """Zero-copy torch view of an env output buffer (float32)."""
+    ptr, shape, _ = env.buffer(which)
+    return torch.as_tensor(_ArrayInterface(ptr, shape), device=torch.device("cuda", torch.cuda.current_device()))
+
+
+def run_env_workload(args, resets: bool, rank: int = 0, world: int = 1, local_rank: int = 0) -> None:
     """The env step path (python/carl.cu:312-370: frameskip ticks, then reward /
     done / transition packing, auto-reset and obs / state packing), timed with
     CUDA events on the env stream, beside the same sequence on the reference's
-    own CUDA build (`carlrefgpu_time_reset_steps`).
+    own CUDA build (`carlrefgpu_time_reset_steps`, rank 0 only).
 
     step:  config C3 (3v3, n_sim sims, seeded floor states), frameskip 8 (the
            gymnasium wrapper's default), discrete actions; env-steps/s.  Team
            sizes, sims and frameskip follow --blue/--orange/--n-sim/--frameskip
            (C2: 1v1, 65536 sims, frameskip 1, so obs are packed every tick).
-    reset: config C5's per-GPU shard (4v4, --reset-n-sim sims, C4 mixed states),
+    c5:    config C5 (4v4, --reset-n-sim sims per GPU, C4 mixed states),
            frameskip 1, each env step followed by a masked apply_reset_state
-           that puts a random 1 % of the sims back to their kickoff state; the
-           fused reset kernel, the separate part kernels (CARLB_FUSED_RESET=0)
-           and the reference run the same sequence, step and reset timed apart."""
+           that puts a random 1 % of the sims back to their kickoff state, and
+           the obs handed to torch (torch's stream waits for the env stream,
+           reads the obs, and the env stream waits for torch before the next
+           step, as the gymnasium wrapper's _sync does).  Every rank steps its
+           own shard (global sim offset rank * n_sim); the value is the whole
+           job's agent-steps/s from the maximum over ranks of the timed steps.
+           On one GPU the separate reset part kernels (CARLB_FUSED_RESET=0)
+           run the same sequence as a second mode."""
     import torch
+    import torch.distributed as dist
 
     from carl_b200 import capi, workloads
 
+    torch.cuda.set_device(local_rank)
     if resets:
         nb = no = 4
         n_sim, frameskip = args.reset_n_sim, 1
@@ -537,7 +674,7 @@ def run_env_workload(args, resets: bool) -> None:
         nb, no = args.blue, args.orange
         n_sim, frameskip = args.n_sim, args.frameskip
     n_cars = nb + no
-    rng = np.random.default_rng(args.seed + 5)
+    rng = np.random.default_rng(args.seed + 5 + 7919 * rank)
     rows = kickoff_rows(n_sim, nb, no, args.seed) if resets else None
     n_steps = args.warmup + args.steps
     masks = (rng.uniform(size=(n_steps, n_sim)) < RESET_FRACTION).astype(np.uint8) if resets else None
@@ -546,11 +683,12 @@ def run_env_workload(args, resets: bool) -> None:
              "car_velocity", "car_angular_velocity", "car_demoed"]
     results = {}
     snap = None
-    for mode in (("fused", "parts") if resets else ("b200",)):
+    modes = ("fused", "parts") if resets and world == 1 else (("fused",) if resets else ("b200",))
+    for mode in modes:
         os.environ["CARLB_FUSED_RESET"] = "0" if mode == "parts" else "1"
-        env = capi.Env(n_sim, nb, no, args.seed, frameskip=frameskip)
+        env = capi.Env(n_sim, nb, no, args.seed, frameskip=frameskip, device=local_rank, sim_offset=rank * n_sim)
         if snap is None:
-            (workloads.mixed_state if resets else workloads.floor_state)(env, args.seed)
+            (workloads.mixed_state if resets else workloads.floor_state)(env, args.seed + 1000 * rank)
             snap = env.snapshot()
         else:
             env.restore(snap)
@@ -558,8 +696,13 @@ def run_env_workload(args, resets: bool) -> None:
         dev = {k: torch.from_numpy(v).cuda() for k, v in rows.items()} if resets else {}
         dmask = torch.from_numpy(masks).cuda() if resets else None
         act = torch.from_numpy(actions).cuda()
+        obs_view = device_view(env, capi.BUF_OBS, torch) if resets else None
+        seen = torch.zeros((), dtype=torch.float32, device="cuda")
         torch.cuda.synchronize()
-        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+        if world > 1:
+            dist.barrier()
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+        current = torch.cuda.current_stream()
         for i in range(n_steps):
             timed = i >= args.warmup
             e = ev[i - args.warmup] if timed else None
@@ -571,38 +714,56 @@ def run_env_workload(args, resets: bool) -> None:
             if resets:
                 env.apply_reset_state(n_sim, *[dev[o] for o in order], True, None, None, dev["blue_score"],
                                       dev["orange_score"], dev["episode_ticks"], reset_mask=dmask[i])
-            if timed:
+                if timed:
+                    e[2].record(stream)
+                # Stream handoff of the obs to torch, and back.
+                current.wait_stream(stream)
+                seen += obs_view[:, :, 0].sum()
+                stream.wait_stream(current)
+            elif timed:
                 e[2].record(stream)
+            if timed:
+                e[3].record(stream)
         env.synchronize()
-        step_ms = sum(a.elapsed_time(b) for a, b, _ in ev) / args.steps
-        reset_ms = sum(b.elapsed_time(c) for _, b, c in ev) / args.steps
-        results[mode] = {"step_ms": step_ms, "reset_ms": reset_ms}
+        torch.cuda.synchronize()
+        step_ms = sum(a.elapsed_time(b) for a, b, _, _ in ev) / args.steps
+        reset_ms = sum(b.elapsed_time(c) for _, b, c, _ in ev) / args.steps
+        handoff_ms = sum(c.elapsed_time(d) for _, _, c, d in ev) / args.steps
+        t = torch.tensor([step_ms, reset_ms, handoff_ms], dtype=torch.float64, device="cuda")
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        results[mode] = {"step_ms": float(t[0]), "reset_ms": float(t[1]), "handoff_ms": float(t[2])}
         env.close()
     os.environ.pop("CARLB_FUSED_RESET", None)
-    try:
-        from oracle.refenv import RefGpu
+    if rank == 0:
+        try:
+            from oracle.refenv import RefGpu
 
-        ref = RefGpu(n_sim, nb, no, args.seed, frameskip=frameskip)
-        ref.restore(snap)
-        if args.warmup:
-            ref.time_reset_steps(capi.ACTIONS_DISCRETE, actions, args.warmup, rows,
-                                 masks[: args.warmup] if resets else None)
-        s_ms, r_ms = ref.time_reset_steps(capi.ACTIONS_DISCRETE, actions, args.steps, rows,
-                                          masks[args.warmup:] if resets else None)
-        ref.close()
-        results["reference_cuda_build"] = {"step_ms": s_ms / args.steps, "reset_ms": r_ms / args.steps}
-    except Exception as exc:  # the reference build is optional here
-        results["reference_cuda_build"] = {"unavailable": str(exc)}
-    for r in results.values():
+            ref = RefGpu(n_sim, nb, no, args.seed, frameskip=frameskip)
+            ref.restore(snap)
+            if args.warmup:
+                ref.time_reset_steps(capi.ACTIONS_DISCRETE, actions, args.warmup, rows,
+                                     masks[: args.warmup] if resets else None)
+            s_ms, r_ms = ref.time_reset_steps(capi.ACTIONS_DISCRETE, actions, args.steps, rows,
+                                              masks[args.warmup:] if resets else None)
+            ref.close()
+            results["reference_cuda_build"] = {"step_ms": s_ms / args.steps, "reset_ms": r_ms / args.steps,
+                                               "handoff_ms": 0.0, "n_gpus": 1}
+        except Exception as exc:  # the reference build is optional here
+            results["reference_cuda_build"] = {"unavailable": str(exc)}
+    if rank != 0:
+        return
+    for name, r in results.items():
         if "step_ms" in r:
-            ms = r["step_ms"] + r["reset_ms"]
-            r["agent_steps_per_s"] = n_sim * n_cars * frameskip / (ms / 1e3)
-            r["env_steps_per_s"] = n_sim / (ms / 1e3)
+            ms = r["step_ms"] + r["reset_ms"] + r["handoff_ms"]
+            gpus = r.get("n_gpus", world)
+            r["agent_steps_per_s"] = n_sim * n_cars * frameskip * gpus / (ms / 1e3)
+            r["env_steps_per_s"] = n_sim * gpus / (ms / 1e3)
     ours = results["fused" if resets else "b200"]
     if resets:
-        metric = "agent-steps/sec, env steps with 1% masked resets per step"
-        workload = (f"C5 per-GPU shard: 4v4 n_sim={n_sim}, frameskip 1, env_step + masked apply_reset_state "
-                    f"of {RESET_FRACTION:.0%} of sims per step")
+        metric = "agent-steps/sec, env steps with 1% masked resets per step and obs handed to torch (C5)"
+        workload = (f"C5 4v4 n_sim={n_sim} per GPU ({n_sim * world} total), frameskip 1, env_step + masked "
+                    f"apply_reset_state of {RESET_FRACTION:.0%} of sims per step + obs stream handoff to torch")
         data = "synthetic (seeded C4 mixed states, discrete actions, random 1% masks, kickoff reset rows)"
     else:
         metric = f"env-steps/sec at {nb}v{no} n_sim={n_sim}, frameskip {frameskip}"
@@ -611,10 +772,10 @@ def run_env_workload(args, resets: bool) -> None:
         data = "synthetic (seeded floor states, discrete actions)"
     line = {
         "metric": metric, "value": ours["agent_steps_per_s"] if resets else ours["env_steps_per_s"],
-        "unit": UNIT if resets else "env-steps/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ours["step_ms"] + ours["reset_ms"], "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": data, "config": {"workload": workload},
-        "modes": results,
+        "unit": UNIT if resets else "env-steps/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ours["step_ms"] + ours["reset_ms"] + ours["handoff_ms"], "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": data,
+        "config": {"workload": workload, "compat_flags": 0}, "modes": results,
     }
     if resets:
         line["gpu_launches_per_reset"] = {"fused": 1, "parts": 8}
@@ -689,13 +850,10 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.workload in ("reset", "step"):
+    if args.workload in ("step", "mask") or (args.workload == "c5" and args.impl == "reference"):
         if rank == 0:
-            run_env_workload(args, resets=args.workload == "reset")
-        return
-    if args.workload == "mask":
-        if rank == 0:
-            run_mask_workload(args)
+            (run_mask_workload(args) if args.workload == "mask"
+             else run_env_workload(args, resets=args.workload == "c5"))
         return
     if args.impl == "reference":
         run_reference(args, rank, world)
@@ -710,7 +868,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_b200(args, rank, world, local_rank)
+        if args.workload == "c5":
+            run_env_workload(args, True, rank, world, local_rank)
+        else:
+            run_b200(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -82,9 +82,11 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> Path:
 def install_arena(source: str | os.PathLike | None = None) -> Path | None:
     """Copies the arena collision mesh next to the library (``_data/arena.obj``).
 
-    The library reads ``$CARL_ARENA_OBJ`` first and falls back to this copy.
+    The mesh comes from ``source`` (the reference's ``assets/arena.obj``) or
+    from ``$CARL_ARENA_OBJ``.  At run time the library reads ``$CARL_ARENA_OBJ``
+    first and falls back to this copy.
     """
-    candidates = [source, os.environ.get("CARL_ARENA_OBJ"), "/root/reference/assets/arena.obj"]
+    candidates = [source, os.environ.get("CARL_ARENA_OBJ")]
     for cand in candidates:
         if cand and Path(cand).is_file():
             DATA.mkdir(exist_ok=True)

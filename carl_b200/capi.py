@@ -24,7 +24,7 @@ ACTIONS_DISCRETE, ACTIONS_CONTINUOUS, ACTIONS_DIRECT = range(3)
  BUF_SCORE_DIFFERENCE, BUF_EPISODE_TICKS, BUF_TRANSITION_SCORE_DIFFERENCE,
  BUF_TRANSITION_EPISODE_TICKS, BUF_OVERTIME, BUF_TRANSITION_OVERTIME) = range(12)
 DT_F32, DT_I32, DT_BOOL, DT_I64 = range(4)
-COMPAT_UNLAGGED_LATERAL_FRICTION = 1
+SOURCE_LAGGED_LATERAL_FRICTION = 1  # compat_flags bit; 0 = the reference CUDA build's semantics
 LIMIT_MAX_TICKS, LIMIT_OVERTIME_TIMEOUT_TICKS, LIMIT_NO_TOUCH_TIMEOUT_TICKS, LIMIT_FRAMESKIP = range(4)
 
 FIELDS = [
@@ -119,6 +119,7 @@ def load() -> ctypes.CDLL:
     lib.carlb_last_tick_ms.argtypes = [vp, ctypes.POINTER(ctypes.c_float)]
     lib.carlb_set_stage_timing.argtypes = [vp, i32]
     lib.carlb_stage_times.argtypes = [vp, ctypes.POINTER(ctypes.c_float), i32, ctypes.POINTER(i32)]
+    lib.carlb_stage_work.argtypes = [vp, ctypes.POINTER(i32)]
     lib.carlb_action_mask.argtypes = [vp, i64, i32, i32, vp, vp]
     _lib = lib
     return lib
@@ -319,6 +320,14 @@ class Env:
         n = ctypes.c_int32()
         self._check(self._lib.carlb_stage_times(self._h, ms, 16, ctypes.byref(n)))
         return {self.STAGES[k]: ms[k] for k in range(n.value)}
+
+    STAGE_WORK = ("plane_cars", "sat_cars", "moving_balls", "car_car_sims")
+
+    def stage_work(self) -> dict[str, int]:
+        """Work-list sizes of the last tick of the last launch (all sim slices)."""
+        counts = (ctypes.c_int32 * 4)()
+        self._check(self._lib.carlb_stage_work(self._h, counts))
+        return {name: int(counts[k]) for k, name in enumerate(self.STAGE_WORK)}
 
     # ---- snapshot ----
     def field_shape(self, name: str) -> tuple[int, int]:

@@ -108,8 +108,9 @@ CB_D bool suspWheel(const Body& body, const SuspFrame& f, int wheel, float dist,
     const float lateralFriction = lateralBase * frictionScale;
     const float longitudinalFriction = longitudinalBase * frictionScale;
 
-    // Coefficients are used one tick after they are computed (see
-    // CARLB_COMPAT_UNLAGGED_LATERAL_FRICTION for the reference build's variant).
+    // The reference's source uses each coefficient one tick after it is computed;
+    // its CUDA build uses the current tick's lateral one (unlaggedLateral, the
+    // default; CARLB_SOURCE_LAGGED_LATERAL_FRICTION selects the source's form).
     const float latUsed = unlaggedLateral ? lateralFriction : latPrev;
     const float lonUsed = lonPrev;
     latPrev = lateralFriction;

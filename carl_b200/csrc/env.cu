@@ -1,7 +1,7 @@
 // carlb_env: one env on one CUDA device behind the C ABI of include/carlb.h.
 //
 // Host orchestration of an RL step (jwmccarthy/CARL python/carl.cu:312-370):
-//   copy actions -> fused tick kernel (frameskip ticks in one launch) ->
+//   copy actions -> stage kernels of frameskip ticks (one graph replay) ->
 //   rewards/dones -> transition state / obs -> auto-reset -> obs, state.
 // Everything is enqueued on the env's own non-blocking stream; the host keeps
 // the tick counter.  Errors are returned as carlb_status with a message; no
@@ -68,7 +68,6 @@ struct carlb_env
     long long carStride = 0, simStride = 0;
     int obsDim = 0, stateDim = 0, actDim = 0;
     cudaStream_t stream = nullptr;
-    int tileSims = 0;
 
     float* car = nullptr;
     float* sim = nullptr;
@@ -94,9 +93,7 @@ struct carlb_env
     int* cellTris = nullptr;
     int hitWords = 1;
 
-    // Tick path: the staged kernel sequence with its scratch (default), or the
-    // fused per-tile kernel (CARLB_TICK_PATH=fused, read at create).
-    bool staged = true;
+    // Scratch of the stage kernels.
     StageScratch scratch{};
     int groups = 2;
     cudaStream_t groupStream[8] = {};
@@ -225,19 +222,6 @@ cudaError_t allocZero(carlb_env* e, T** p, size_t count)
     return cudaMemsetAsync(v, 0, count * sizeof(T), e->stream);
 }
 
-int chooseTileSims(int nCars, int hitWords)
-{
-    if (const char* s = std::getenv("CARLB_TILE_SIMS"))
-    {
-        const int v = std::atoi(s);
-        if (v > 0 && v * nCars <= 256) return v;
-    }
-    int best = 1;
-    for (int ts = 1; ts <= 64 && ts * nCars <= 256; ts++)
-        if (tickSmemBytes(ts, nCars, hitWords, tickThreads(ts, nCars)) <= 112 * 1024) best = ts;
-    return best;
-}
-
 size_t actionRowBytes(carlb_action_kind kind) { return kind == CARLB_ACTIONS_DIRECT ? 32 : 28; }
 
 // hostIn: the actions are being copied in per slice on the copy stream
@@ -261,12 +245,11 @@ carlb_status launchTicks(carlb_env* e, carlb_action_kind kind, int nTicks, bool 
     p.seed = e->cfg.seed;
     p.tick0 = e->tick;
     p.nTicks = nTicks;
-    p.tileSims = e->tileSims;
     p.compatFlags = e->cfg.compat_flags;
     // A caller capturing the env stream into its own graph gets the kernels in that capture.
     cudaStreamCaptureStatus outer = cudaStreamCaptureStatusNone;
     ECHECK(e, cudaStreamIsCapturing(e->stream, &outer));
-    if (e->staged && e->useGraph && nTicks > 0 && outer == cudaStreamCaptureStatusNone)
+    if (e->useGraph && nTicks > 0 && outer == cudaStreamCaptureStatusNone)
     {
         cudaGraphExec_t exec = nullptr;
         for (const auto& g : e->graphs)
@@ -307,11 +290,9 @@ carlb_status launchTicks(carlb_env* e, carlb_action_kind kind, int nTicks, bool 
         }
     }
     ECHECK(e, cudaEventRecord(e->ev0, e->stream));
-    const int err = e->staged
-        ? launchTickStaged(p, e->arena(), e->scratch, e->stream, e->stageStreams(hostIn))
-        : launchTick(p, e->arena(), e->stream);
+    const int err = launchTickStaged(p, e->arena(), e->scratch, e->stream, e->stageStreams(hostIn));
     if (err) return cudaFail(e, (cudaError_t)err, "tick kernel launch");
-    e->stageTimed = e->staged && e->stageTiming && nTicks > 0;
+    e->stageTimed = e->stageTiming && nTicks > 0;
     ECHECK(e, cudaEventRecord(e->ev1, e->stream));
     e->tick += nTicks;
     return CARLB_OK;
@@ -491,10 +472,10 @@ static carlb_status initEnv(carlb_env* p, const carlb_config* cfg)
     p->stateDim = packedStateDim(p->nCars);
     p->actDim = p->nCars * ACT_PER_CAR;
     p->hitWords = (host->maxCellTris + 31) / 32;
-    p->tileSims = chooseTileSims(p->nCars, p->hitWords);
-    // Pad to whole tiles (rounded to 4 rows) so every per-word row is 16-byte aligned.
-    const long long simPad = ((long long)cfg->n_sim + p->tileSims - 1) / p->tileSims * p->tileSims;
-    p->simStride = (simPad + 3) / 4 * 4;
+    // Rows padded to whole warps of sims (and 4 words), so every per-word row is
+    // 16-byte aligned.
+    const long long simPad = ((long long)cfg->n_sim + 31) / 32 * 32;
+    p->simStride = simPad;
     p->carStride = (simPad * p->nCars + 3) / 4 * 4;
 
     ECHECK(p, cudaSetDevice(cfg->device));
@@ -521,11 +502,6 @@ static carlb_status initEnv(carlb_env* p, const carlb_config* cfg)
     if (const char* fr = std::getenv("CARLB_FUSED_RESET")) p->fusedReset = std::atoi(fr) != 0;
     if (const char* sp = std::getenv("CARLB_STAGED_PACK")) p->stagedPack = std::atoi(sp) != 0;
     if (const char* fe = std::getenv("CARLB_FUSED_EPILOGUE")) p->fusedEpilogue = std::atoi(fe) != 0;
-    {
-        const char* path = std::getenv("CARLB_TICK_PATH");
-        p->staged = !(path && std::string(path) == "fused");
-    }
-    if (p->staged)
     {
         if (const char* g = std::getenv("CARLB_GROUPS")) p->groups = std::max(1, std::min(8, std::atoi(g)));
         // Slices of fewer than ~4k sims would leave the wide stages too small.
@@ -560,6 +536,8 @@ static carlb_status initEnv(carlb_env* p, const carlb_config* cfg)
         ECHECK(p, allocZero(p, &p->scratch.ball, (size_t)15 * p->simStride));
         ECHECK(p, allocZero(p, &p->scratch.ballList, (size_t)p->simStride));
         ECHECK(p, allocZero(p, &p->scratch.ballCount, (size_t)8));
+        ECHECK(p, allocZero(p, &p->scratch.ccCount, (size_t)8));
+        ECHECK(p, allocZero(p, &p->scratch.stats, (size_t)8 * STAGE_WORK));
     }
     p->actionCapacity = (size_t)p->nCarTotal * 32;
     {
@@ -721,6 +699,16 @@ static carlb_status initEnv(carlb_env* p, const carlb_config* cfg)
     buildTables(tables);
     ECHECK(p, (cudaError_t)uploadTickTables(tables));
     ECHECK(p, (cudaError_t)uploadEnvioTables(tables));
+    {
+        // Set-up for carlb_ticks_static_scratch, once per device: look up the fixed
+        // scratch array and load the stage kernels, so that entry point's calls
+        // allocate nothing.
+        void* base = nullptr;
+        void* lastUse = nullptr;
+        size_t capacity = 0;
+        if (const int serr = staticScratchAddress(&base, &capacity, &lastUse))
+            return cudaFail(p, (cudaError_t)serr, "static scratch set-up");
+    }
 
     const carlb_status st = resetEnv(p);
     if (st != CARLB_OK) return st;
@@ -740,6 +728,8 @@ carlb_status carlb_create(const carlb_config* cfg, carlb_env** out)
         return fail(nullptr, CARLB_ERR_VALUE, "at most 4 cars per team (4 kickoff spots per team)");
     if (cfg->frameskip < 1) return fail(nullptr, CARLB_ERR_VALUE, "frameskip must be at least 1");
     if (cfg->sim_offset < 0) return fail(nullptr, CARLB_ERR_VALUE, "sim_offset must be non-negative");
+    if (cfg->compat_flags & ~CARLB_SOURCE_LAGGED_LATERAL_FRICTION)
+        return fail(nullptr, CARLB_ERR_VALUE, "unknown compat_flags bits");
 
     carlb_env* p = new carlb_env;
     const carlb_status st = initEnv(p, cfg);
@@ -807,11 +797,20 @@ carlb_status carlb_ticks_static_scratch(carlb_env* e, carlb_action_kind kind, co
 {
     if (!e) return fail(nullptr, CARLB_ERR_VALUE, "env is null");
     if (n < 0) return fail(e, CARLB_ERR_VALUE, "n_ticks must be non-negative");
-    if (!e->staged) return fail(e, CARLB_ERR_STATE, "the static-scratch ticks need the staged tick path");
+    // The caller's current device is restored on return (the address lookup and
+    // the launches need the env's device current).
+    int callerDevice = -1;
+    ECHECK(e, cudaGetDevice(&callerDevice));
+    struct RestoreDevice
+    {
+        int dev;
+        ~RestoreDevice() { cudaSetDevice(dev); }
+    } restore{ callerDevice };
     ECHECK(e, cudaSetDevice(e->cfg.device));
     void* base = nullptr;
+    void* lastUse = nullptr;
     size_t capacity = 0;
-    const int aerr = staticScratchAddress(&base, &capacity);
+    const int aerr = staticScratchAddress(&base, &capacity, &lastUse);
     if (aerr) return cudaFail(e, (cudaError_t)aerr, "static scratch lookup");
 
     // Carve the stage scratch out of the fixed array (each part 256-byte aligned).
@@ -826,7 +825,7 @@ carlb_status carlb_ticks_static_scratch(carlb_env* e, carlb_action_kind kind, co
     const size_t oHits = take((size_t)e->hitWords * cs * 4), oWheel = take(cs * 4), oKeys = take(4 * cs * 8);
     const size_t oHeavyBody = take(18 * cs * 4), oHeavyList = take((size_t)HEAVY_CLASSES * cs * 4);
     const size_t oHeavyCount = take(8 * HEAVY_CLASSES * 4), oBall = take(15 * ss * 4), oBallList = take(ss * 4);
-    const size_t oBallCount = take(8 * 4);
+    const size_t oBallCount = take(8 * 4), oCcCount = take(8 * 4), oStats = take(8 * STAGE_WORK * 4);
     if (off > capacity)
         return fail(e, CARLB_ERR_VALUE,
                     "env needs " + std::to_string(off) + " bytes of stage scratch; the static scratch holds " +
@@ -845,13 +844,23 @@ carlb_status carlb_ticks_static_scratch(carlb_env* e, carlb_action_kind kind, co
     x.ball = reinterpret_cast<float*>(b + oBall);
     x.ballList = reinterpret_cast<int*>(b + oBallList);
     x.ballCount = reinterpret_cast<int*>(b + oBallCount);
+    x.ccCount = reinterpret_cast<int*>(b + oCcCount);
+    x.stats = reinterpret_cast<int*>(b + oStats);
 
     carlb_status s = stageActions(e, kind, actions, cudaMemcpyDeviceToDevice);
     if (s != CARLB_OK) return s;
+    // One call at a time uses the array: the env stream waits for the end of the
+    // work the previous call enqueued (any env, any stream), and this call's end
+    // is recorded in its place.  The lock keeps the wait and the record of
+    // concurrent host threads in one order.
+    static std::mutex order;
+    std::lock_guard<std::mutex> guard(order);
+    ECHECK(e, cudaStreamWaitEvent(e->stream, (cudaEvent_t)lastUse, 0));
     // The work-list counters start at zero (every other scratch word is written
     // before it is read within a tick).
     ECHECK(e, cudaMemsetAsync(x.heavyCount, 0, 8 * HEAVY_CLASSES * 4, e->stream));
     ECHECK(e, cudaMemsetAsync(x.ballCount, 0, 8 * 4, e->stream));
+    ECHECK(e, cudaMemsetAsync(x.ccCount, 0, 8 * 4, e->stream));
 
     TickParams p{};
     p.car = e->car;
@@ -870,14 +879,16 @@ carlb_status carlb_ticks_static_scratch(carlb_env* e, carlb_action_kind kind, co
     p.seed = e->cfg.seed;
     p.tick0 = e->tick;
     p.nTicks = n;
-    p.tileSims = e->tileSims;
     p.compatFlags = e->cfg.compat_flags;
     StageStreams streams = e->stageStreams();
     for (int k = 0; k < 2 * STAGE_KERNELS; k++) streams.stageEvents[k] = nullptr;
     ECHECK(e, cudaEventRecord(e->ev0, e->stream));
     const int err = launchTickStaged(p, e->arena(), x, e->stream, streams);
+    e->stageTimed = false;  // this call records no stage events
     if (err) return cudaFail(e, (cudaError_t)err, "tick kernel launch");
     ECHECK(e, cudaEventRecord(e->ev1, e->stream));
+    // Every stage kernel of the launch has joined the env stream by here.
+    ECHECK(e, cudaEventRecord((cudaEvent_t)lastUse, e->stream));
     e->tick += n;
     return CARLB_OK;
 }
@@ -889,7 +900,7 @@ carlb_status carlb_ticks_host(carlb_env* e, carlb_action_kind kind, const void* 
     if (n < 0) return fail(e, CARLB_ERR_VALUE, "n_ticks must be non-negative");
     cudaStreamCaptureStatus outer = cudaStreamCaptureStatusNone;
     ECHECK(e, cudaStreamIsCapturing(e->stream, &outer));
-    const bool sliced = e->staged && e->overlapCopy && n > 0 && outer == cudaStreamCaptureStatusNone;
+    const bool sliced = e->overlapCopy && n > 0 && outer == cudaStreamCaptureStatusNone;
     carlb_status s = sliced ? stageHostActionsSliced(e, kind, hostActions)
                             : stageActions(e, kind, hostActions, cudaMemcpyHostToDevice);
     if (s != CARLB_OK) return s;
@@ -1184,7 +1195,6 @@ carlb_status carlb_write_field(carlb_env* e, carlb_field field, const void* in)
 carlb_status carlb_set_stage_timing(carlb_env* e, int32_t enabled)
 {
     if (!e) return fail(nullptr, CARLB_ERR_VALUE, "env is null");
-    if (!e->staged) return fail(e, CARLB_ERR_STATE, "stage timing needs the staged tick path");
     ECHECK(e, cudaSetDevice(e->cfg.device));
     for (int k = 0; k < 2 * STAGE_KERNELS && enabled; k++)
         if (!e->stageEv[k]) ECHECK(e, cudaEventCreate(&e->stageEv[k]));
@@ -1203,6 +1213,22 @@ carlb_status carlb_stage_times(carlb_env* e, float* ms, int32_t capacity, int32_
         ECHECK(e, cudaEventSynchronize(e->stageEv[2 * k + 1]));
         ECHECK(e, cudaEventElapsedTime(&ms[k], e->stageEv[2 * k], e->stageEv[2 * k + 1]));
         *count = k + 1;
+    }
+    return CARLB_OK;
+}
+
+carlb_status carlb_stage_work(carlb_env* e, int32_t counts[4])
+{
+    if (!e) return fail(nullptr, CARLB_ERR_VALUE, "env is null");
+    if (!counts) return fail(e, CARLB_ERR_VALUE, "counts is null");
+    ECHECK(e, cudaSetDevice(e->cfg.device));
+    ECHECK(e, cudaStreamSynchronize(e->stream));
+    int host[8 * STAGE_WORK] = {};
+    ECHECK(e, cudaMemcpy(host, e->scratch.stats, sizeof(host), cudaMemcpyDeviceToHost));
+    for (int k = 0; k < STAGE_WORK; k++)
+    {
+        counts[k] = 0;
+        for (int g = 0; g < 8; g++) counts[k] += host[g * STAGE_WORK + k];
     }
     return CARLB_OK;
 }

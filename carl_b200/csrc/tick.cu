@@ -1,29 +1,26 @@
-// Fused tick kernel.
+// The batched tick as a sequence of sm_100a stage kernels.
 //
-// One CTA owns a tile of `tileSims` consecutive sims.  It copies the tile's
-// persistent state (76 words per car, 66 per sim) from HBM into shared memory
-// once, runs `nTicks` complete ticks on it, and copies it back once: between
-// ticks nothing leaves the SM.  Within a tick the stages run in the
-// reference's order (jwmccarthy/CARL src/RLEnvironment.cu:166-211):
+// Every stage kernel works on the persistent state in global memory (word-major
+// SoA, resident in the 126 MB L2 between stages), so each stage runs at its own
+// occupancy and no warp waits on a CTA barrier for unrelated work.  Within a tick
+// the stages run in the reference's order (jwmccarthy/CARL src/Kernels.cu:15-202,
+// src/RLEnvironment.cu:166-211):
 //
 //   begin step -> broadphase -> suspension raycast -> controls -> SAT/clip ->
 //   suspension + manifold + solve -> car-car -> ball (arena, cars, integrate,
 //   goal) -> integrate cars -> finish tick (impulses, demo respawn) -> pads
 //
-// and are mapped onto the CTA as
-//   * per-car stages: one thread per car;
-//   * the (car, candidate triangle) work of raycast and SAT: flattened over the
-//     whole tile with a block scan and spread evenly over all threads (cells hold
-//     0-262 triangles, so per-car loops would leave most lanes idle); the wheel
-//     ray minimum is an atomicMin on (distance bits, candidate) keys, which picks
-//     the same triangle as the reference's first-minimum scan; SAT hits are a
-//     per-car bitmask of candidate numbers, processed in candidate order;
-//   * per-sim stages (car-car pairs, ball): one warp per sim; pair gates, ball
-//     triangle tests and ball-car gates run across lanes, the order-dependent
-//     solves on lane 0.
-// All physics arithmetic lives in cb_*.cuh and keeps the reference's fp32
-// operation order (the file is compiled with --fmad=false).
+// The (car, candidate triangle) work of the raycasts and the SAT is flattened over
+// a CTA with a block scan and spread evenly over its threads (cells hold 0-262
+// triangles, so per-car loops would leave most lanes idle); the wheel ray minimum
+// is an atomicMin on (distance bits, candidate) keys, which picks the same
+// triangle as the reference's first-minimum scan; SAT hits are a per-car bitmask
+// of candidate numbers, processed in candidate order.  All physics arithmetic
+// lives in cb_*.cuh and keeps the reference's fp32 operation order (the file is
+// compiled with --fmad=false).
 #include "tick.cuh"
+
+#include "../../include/carlb.h"
 
 #include <algorithm>
 #include <mutex>
@@ -39,35 +36,6 @@ namespace {
 constexpr int WARP_HIT_BUF = 256;    // ball-arena triangle hits gathered per warp
 constexpr int WARP_WORDS = WARP_HIT_BUF + 8;
 constexpr unsigned FULL = 0xffffffffu;
-
-struct Layout
-{
-    int TC, TS, W, HW;
-    int cw, sw, cell, cnt, pre, rs, hits, wsum, key, warp, total;
-};
-
-CB_HD Layout layoutOf(int tileSims, int nCars, int hitWords, int threads)
-{
-    Layout L;
-    L.TS = tileSims;
-    L.TC = tileSims * nCars;
-    L.W = threads / 32;
-    L.HW = hitWords;
-    int o = 0;
-    L.cw = o;   o += NCW * L.TC;
-    L.sw = o;   o += NSW * L.TS;
-    L.cell = o; o += L.TC;
-    L.cnt = o;  o += L.TC;
-    L.pre = o;  o += L.TC + 1;
-    L.rs = o;   o += 15 * L.TC;
-    L.hits = o; o += L.HW * L.TC;
-    L.wsum = o; o += 32;
-    o = (o + 1) & ~1;  // 8-byte alignment for the 64-bit keys
-    L.key = o;  o += 8 * L.TC;
-    L.warp = o; o += L.W * WARP_WORDS;
-    L.total = o;
-    return L;
-}
 
 __device__ __forceinline__ float rayLen(int w) { return suspRayLength(w); }
 
@@ -413,21 +381,6 @@ __device__ V3 ballArenaSolve(const SmemSoa& cars, const SmemSoa& sims, int s, in
     return pushVel;
 }
 
-// Part 1 for one sim on one warp (fused path): prelude, arena contacts, hand-over.
-__device__ void ballArenaStage(const SmemSoa& cars, const SmemSoa& sims, int s, int nCars, int tick,
-                               const ArenaDev& arena, int* wbuf, int lane, float* scratch, int scratchStride)
-{
-    const BallPre b = ballPre(sims, s);
-    V3 pushVel = v3zero();
-    if (!b.sleeping) pushVel = ballArenaSolve(cars, sims, s, nCars, tick, arena, wbuf, lane, b);
-    if (lane == 0)
-    {
-        const V3 out[5] = { b.exportedPos, b.posBT, b.preSolveBT, pushVel, b.velNoExt };
-        storeBallScratch(scratch, scratchStride, s, out, 0, 5);
-    }
-    __syncwarp();
-}
-
 // ---- ball stage, part 2: ball vs cars (in car order), integration, goal; one thread ----------
 __device__ void ballFinishStage(const SmemSoa& cars, const SmemSoa& sims, int s, int nCars, int tick,
                                 const float* scratch, int scratchStride)
@@ -469,570 +422,8 @@ __device__ void ballFinishStage(const SmemSoa& cars, const SmemSoa& sims, int s,
     detectGoal(sims, s, ballPos, tick);
 }
 
-// ---- the kernel -------------------------------------------------------------------------
-
-__global__ void __launch_bounds__(256) tickKernel(TickParams p, ArenaDev arena)
-{
-    extern __shared__ __align__(16) float smem[];
-    const int tid = threadIdx.x;
-    const int lane = tid & 31;
-    const int warp = tid >> 5;
-    const int nCars = p.nCars;
-    const Layout L = layoutOf(p.tileSims, nCars, arena.hitWords, blockDim.x);
-    const int simBase = blockIdx.x * p.tileSims;
-    const int simsHere = min(p.tileSims, p.nSim - simBase);
-    const int carsHere = simsHere * nCars;
-    const long long carBase = (long long)simBase * nCars;
-
-    const SmemSoa cars{ smem + L.cw, L.TC };
-    const SmemSoa sims{ smem + L.sw, L.TS };
-    int* cellS = reinterpret_cast<int*>(smem + L.cell);
-    int* cntS = reinterpret_cast<int*>(smem + L.cnt);
-    int* preS = reinterpret_cast<int*>(smem + L.pre);
-    float* rsS = smem + L.rs;
-    unsigned* hitS = reinterpret_cast<unsigned*>(smem + L.hits);
-    int* wsumS = reinterpret_cast<int*>(smem + L.wsum);
-    unsigned long long* keyS = reinterpret_cast<unsigned long long*>(smem + L.key);
-    int* wbuf = reinterpret_cast<int*>(smem + L.warp) + warp * WARP_WORDS;
-
-    // ---- load the tile ----
-    for (int w = 0; w < NCW; w++)
-        for (int i = tid; i < carsHere; i += blockDim.x)
-            cars.f(w, i) = p.car[(long long)w * p.carStride + carBase + i];
-    for (int w = 0; w < NSW; w++)
-        for (int i = tid; i < simsHere; i += blockDim.x)
-            sims.f(w, i) = p.sim[(long long)w * p.simStride + simBase + i];
-
-    const bool carThread = tid < carsHere;
-    const int mySim = carThread ? tid / nCars : 0;
-    const int myLocal = carThread ? tid - mySim * nCars : 0;
-    Controls ctl{};
-    if (carThread) ctl = decodeAction(p.actions, p.actionKind, carBase + tid);
-    unsigned wheelContactBits = 0;
-    bool respawned = false;
-    __syncthreads();
-
-    for (int t = 0; t < p.nTicks; t++)
-    {
-        const int tick = p.tick0 + t + 1;
-        const bool lastTick = t == p.nTicks - 1;
-
-        // ---- begin step + broadphase ----
-        if (tid < simsHere) sims.n(S_EP_TICKS, tid) += 1;
-        if (carThread)
-        {
-            const V3 pos = cars.v(C_POS, tid), vel = cars.v(C_VEL, tid), ang = cars.v(C_ANG, tid);
-            const V3 cen = cars.v(C_CEN, tid);
-            const Q4 rot = cars.q(C_ROT, tid);
-            const int cell = broadphaseCell(pos, vel, ang, cen, rot);
-            const int first = __ldg(&arena.cellStart[cell]);
-            cellS[tid] = first;  // first entry of the car's candidate list
-            cntS[tid] = __ldg(&arena.cellStart[cell + 1]) - first;
-            if (lastTick && p.diagCar) p.diagCar[0 * p.carStride + carBase + tid] = cell;
-            const V3 up = rotate(rot, axisVec(2));
-            #pragma unroll
-            for (int w = 0; w < NUM_WHEELS; w++)
-            {
-                const V3 st = cen + rotate(rot, suspConnection(w));
-                rsS[(3 * w) * L.TC + tid] = st.x;
-                rsS[(3 * w + 1) * L.TC + tid] = st.y;
-                rsS[(3 * w + 2) * L.TC + tid] = st.z;
-                keyS[4 * tid + w] = rayKey(rayLen(w) + 1.f, 0xffffffffu);
-            }
-            const V3 dir = neg(up);
-            rsS[12 * L.TC + tid] = dir.x;
-            rsS[13 * L.TC + tid] = dir.y;
-            rsS[14 * L.TC + tid] = dir.z;
-            for (int h = 0; h < L.HW; h++) hitS[h * L.TC + tid] = 0u;
-        }
-        else if (tid < L.TC)
-        {
-            cntS[tid] = 0;
-        }
-
-        // ---- block exclusive scan of candidate counts ----
-        {
-            int v = tid < carsHere ? cntS[tid] : 0;
-            #pragma unroll
-            for (int d = 1; d < 32; d <<= 1)
-            {
-                const int u = __shfl_up_sync(FULL, v, d);
-                if (lane >= d) v += u;
-            }
-            if (lane == 31) wsumS[warp] = v;
-            __syncthreads();
-            if (warp == 0)
-            {
-                int s = lane < L.W ? wsumS[lane] : 0;
-                #pragma unroll
-                for (int d = 1; d < 32; d <<= 1)
-                {
-                    const int u = __shfl_up_sync(FULL, s, d);
-                    if (lane >= d) s += u;
-                }
-                if (lane < L.W) wsumS[lane] = s;
-            }
-            __syncthreads();
-            if (warp > 0) v += wsumS[warp - 1];
-            if (tid < carsHere) preS[tid + 1] = v;
-            if (tid == 0) preS[0] = 0;
-        }
-        __syncthreads();
-
-        // ---- flattened (car, candidate) work: wheel rays and SAT ----
-        const int total = preS[carsHere];
-        if (tid == 0)
-        {
-            // Solve-order counters for the next stage (the scan's sums are dead now).
-            wsumS[1] = 0;
-            wsumS[2] = 0;
-        }
-        for (int it = tid; it < total; it += blockDim.x)
-        {
-            int lo = 0, hi = carsHere - 1;
-            while (lo < hi)
-            {
-                const int mid = (lo + hi + 1) >> 1;
-                if (preS[mid] <= it) lo = mid;
-                else hi = mid - 1;
-            }
-            const int c = lo;
-            const int k = it - preS[c];
-            const int e = cellS[c] + k;
-            {
-                // Triangles out of reach of the box and the wheel rays cannot
-                // produce a ray hit or a SAT overlap.
-                const float4 sph = __ldg(&arena.cellSph[e]);
-                const V3 cc = cars.v(C_CEN, c);
-                const float dx = sph.x - cc.x, dy = sph.y - cc.y, dz = sph.z - cc.z;
-                const float rr = sph.w + arena.carReach;
-                if (dx * dx + dy * dy + dz * dz > rr * rr) continue;
-            }
-            const int tri = __ldg(&arena.cellTris[e]);
-            V3 v0, v1, v2;
-            int flags;
-            loadTri(arena, tri, v0, v1, v2, flags);
-
-            // Wheel rays (Moller-Trumbore).
-            const V3 dir = { rsS[12 * L.TC + c], rsS[13 * L.TC + c], rsS[14 * L.TC + c] };
-            const V3 e1 = v1 - v0;
-            const V3 e2 = v2 - v0;
-            const V3 pv = cross(dir, e2);
-            const float det = dot(e1, pv);
-            if (!(fabsf(det) < RAY_PARALLEL_EPS))
-            {
-                const float invDet = 1.f / det;
-                #pragma unroll
-                for (int w = 0; w < NUM_WHEELS; w++)
-                {
-                    const V3 st = { rsS[(3 * w) * L.TC + c], rsS[(3 * w + 1) * L.TC + c], rsS[(3 * w + 2) * L.TC + c] };
-                    const V3 tv = st - v0;
-                    const float u = invDet * dot(tv, pv);
-                    if (u < 0.f || u > 1.f) continue;
-                    const V3 qv = cross(tv, e1);
-                    const float v = invDet * dot(dir, qv);
-                    if (v < 0.f || u + v > 1.f) continue;
-                    const float dist = invDet * dot(e2, qv);
-                    if (dist <= 0.f || !(dist < rayLen(w) + 1.f)) continue;
-                    atomicMin(&keyS[4 * c + w], rayKey(dist, (unsigned)k));
-                }
-            }
-
-            // Car-vs-triangle SAT (analytic planes are handled by the manifold).
-            if (!(flags & 1))
-            {
-                const LocalTri lt = localTriangle(cars.v(C_CEN, c), cars.q(C_ROT, c), v0, v1, v2);
-                if (carTriSat(lt).overlap) atomicOr(&hitS[(k >> 5) * L.TC + c], 1u << (k & 31));
-            }
-        }
-        __syncthreads();
-
-        // ---- per car: finish wheel rays, controls ----
-        float rayDist[NUM_WHEELS];
-        V3 rayNormal[NUM_WHEELS];
-        if (carThread)
-        {
-            const int i = tid;
-            const V3 cen = cars.v(C_CEN, i);
-            const Q4 rot = cars.q(C_ROT, i);
-            const V3 up = rotate(rot, axisVec(2));
-            const V3 dir = neg(up);
-            int src[NUM_WHEELS];
-            V3 start[NUM_WHEELS];
-            const int cellFirst = cellS[i];
-            #pragma unroll
-            for (int w = 0; w < NUM_WHEELS; w++)
-            {
-                start[w] = V3{ rsS[(3 * w) * L.TC + i], rsS[(3 * w + 1) * L.TC + i], rsS[(3 * w + 2) * L.TC + i] };
-                const unsigned long long key = keyS[4 * i + w];
-                const unsigned cand = (unsigned)(key & 0xffffffffu);
-                if (cand != 0xffffffffu)
-                {
-                    rayDist[w] = __uint_as_float((unsigned)(key >> 32));
-                    V3 v0, v1, v2;
-                    int flags;
-                    loadTri(arena, __ldg(&arena.cellTris[cellFirst + (int)cand]), v0, v1, v2, flags);
-                    V3 n = cross(v1 - v0, v2 - v0);
-                    const float nl = lensq(n);
-                    n = n * rsqrtf(nl);
-                    if (dot(n, dir) > 0.f) n = neg(n);
-                    rayNormal[w] = n;
-                    src[w] = WHEEL_ARENA;
-                }
-                else
-                {
-                    rayDist[w] = rayLen(w) + 1.f;
-                    rayNormal[w] = up;
-                    src[w] = WHEEL_NONE;
-                }
-            }
-            // Other cars' boxes, in car order.
-            const int sb = mySim * nCars;
-            for (int k = 0; k < nCars; k++)
-            {
-                const int o = sb + k;
-                if (o == i || cars.n(C_DEMOED, o)) continue;
-                const V3 oc = cars.v(C_CEN, o);
-                if (lensq(oc - cen) > 250.f * 250.f) continue;  // beyond any wheel ray + box reach
-                const Q4 orot = cars.q(C_ROT, o);
-                #pragma unroll
-                for (int w = 0; w < NUM_WHEELS; w++)
-                {
-                    const V3 ls = unrotate(orot, start[w] - oc);
-                    const V3 ld = unrotate(orot, dir);
-                    float entry = 0.f, exitD = rayLen(w);
-                    int hitAxis = -1;
-                    bool miss = false;
-                    #pragma unroll
-                    for (int a = 0; a < 3; a++)
-                    {
-                        const float h = vget(carHalfExtents(), a);
-                        const float d = vget(ld, a), s0 = vget(ls, a);
-                        if (fabsf(d) < RAY_PARALLEL_EPS)
-                        {
-                            if (fabsf(s0) > h) { miss = true; break; }
-                            continue;
-                        }
-                        const float inv = 1.f / d;
-                        const float t1 = (-h - s0) * inv;
-                        const float t2 = (h - s0) * inv;
-                        const float tn = fminf(t1, t2);
-                        if (tn > entry)
-                        {
-                            entry = tn;
-                            hitAxis = a;
-                        }
-                        exitD = fminf(exitD, fmaxf(t1, t2));
-                        if (entry > exitD) { miss = true; break; }
-                    }
-                    if (miss || hitAxis < 0 || entry >= rayDist[w]) continue;
-                    V3 ln = v3zero();
-                    vset(ln, hitAxis, vget(ld, hitAxis) > 0.f ? -1.f : 1.f);
-                    rayDist[w] = entry;
-                    rayNormal[w] = rotate(orot, ln);
-                    src[w] = WHEEL_CAR;
-                }
-            }
-            // Ball.
-            {
-                const V3 bp = sims.v(S_BPOS, mySim);
-                const float invR = 1.f / BALL_COLLISION_RADIUS;
-                #pragma unroll
-                for (int w = 0; w < NUM_WHEELS; w++)
-                {
-                    const V3 off = start[w] - bp;
-                    const float b = dot(off, dir);
-                    const float cc = lensq(off) - BALL_COLLISION_RADIUS * BALL_COLLISION_RADIUS;
-                    if (cc < 0.f) continue;
-                    const float disc = b * b - cc;
-                    if (disc < 0.f) continue;
-                    const float dist = -b - sqrtf(disc);
-                    if (!(dist > 0.f && dist <= rayLen(w))) continue;
-                    if (dist >= rayDist[w]) continue;
-                    rayDist[w] = dist;
-                    rayNormal[w] = (start[w] + dir * dist - bp) * invR;
-                    src[w] = WHEEL_BALL;
-                }
-            }
-            wheelContactBits = 0;
-            #pragma unroll
-            for (int w = 0; w < NUM_WHEELS; w++)
-                if (src[w] != WHEEL_NONE && rayDist[w] <= rayLen(w)) wheelContactBits |= 1u << w;
-            if (lastTick)
-            {
-                #pragma unroll
-                for (int w = 0; w < NUM_WHEELS; w++)
-                {
-                    const long long g = carBase + i;
-                    p.carOut[(long long)(O_RAY_DIST + w) * p.carStride + g] = rayDist[w];
-                    p.carOut[(long long)(O_RAY_NORMAL + 3 * w) * p.carStride + g] = rayNormal[w].x;
-                    p.carOut[(long long)(O_RAY_NORMAL + 3 * w + 1) * p.carStride + g] = rayNormal[w].y;
-                    p.carOut[(long long)(O_RAY_NORMAL + 3 * w + 2) * p.carStride + g] = rayNormal[w].z;
-                    reinterpret_cast<int*>(p.carOut)[(long long)(O_WHEEL_SRC + w) * p.carStride + g] = src[w];
-                }
-            }
-
-            // Controls.
-            V3 vel = cars.v(C_VEL, i), ang = cars.v(C_ANG, i);
-            Internal s = loadInternal(cars, i);
-            Susp su = loadSusp(cars, i);
-            processControls(ctl, cars.n(C_DEMOED, i) != 0, rot, vel, ang, s, su, rayDist,
-                            cars.n(C_MAN_COUNT, i), cars.v(C_MAN_N0, i));
-            cars.setv(C_VEL, i, vel);
-            cars.setv(C_ANG, i, ang);
-            storeInternal(cars, i, s);
-            storeSusp(cars, i, su);
-
-            // Hand the ray results to whichever thread solves this car: the
-            // distances go into the car's own (already consumed) ray keys, the
-            // normals over its own ray starts.
-            float* rd = reinterpret_cast<float*>(keyS) + 8 * i;
-            #pragma unroll
-            for (int w = 0; w < NUM_WHEELS; w++)
-            {
-                rd[w] = rayDist[w];
-                rsS[(3 * w) * L.TC + i] = rayNormal[w].x;
-                rsS[(3 * w + 1) * L.TC + i] = rayNormal[w].y;
-                rsS[(3 * w + 2) * L.TC + i] = rayNormal[w].z;
-            }
-            // Solve order: cars likely to have mesh or plane contacts first, so the
-            // long contact path runs in as few warps as possible.
-            bool heavy = false;
-            if (!cars.n(C_DEMOED, i))
-            {
-                heavy = cars.n(C_MAN_COUNT, i) > 0;
-                for (int h = 0; h < L.HW && !heavy; h++) heavy = hitS[h * L.TC + i] != 0u;
-            }
-            const int slot = heavy ? atomicAdd(&wsumS[1], 1) : carsHere - 1 - atomicAdd(&wsumS[2], 1);
-            preS[slot] = i;
-        }
-        __syncthreads();  // every ray has read the other cars' poses
-
-        // ---- per car (in solve order): SAT contacts, suspension, manifold, solve ----
-        if (carThread)
-        {
-            const int i = preS[tid];
-            {
-                const float* rd = reinterpret_cast<const float*>(keyS) + 8 * i;
-                #pragma unroll
-                for (int w = 0; w < NUM_WHEELS; w++)
-                {
-                    rayDist[w] = rd[w];
-                    rayNormal[w] = V3{ rsS[(3 * w) * L.TC + i], rsS[(3 * w + 1) * L.TC + i], rsS[(3 * w + 2) * L.TC + i] };
-                }
-            }
-            const V3 cen = cars.v(C_CEN, i);
-            const Q4 rot = cars.q(C_ROT, i);
-            const int cellFirst = cellS[i];
-            const int nCand = cntS[i];
-
-            if (lastTick && p.diagCar)
-            {
-                const long long g = carBase + i;
-                p.diagCar[1 * p.carStride + g] = nCand;
-                int nh = 0;
-                for (int h = 0; h < L.HW && nh < MAX_CAR_TRI_PAIRS; h++)
-                    for (unsigned m = hitS[h * L.TC + i]; m && nh < MAX_CAR_TRI_PAIRS; m &= m - 1)
-                    {
-                        const int k = h * 32 + __ffs(m) - 1;
-                        p.diagCar[(3 + nh) * p.carStride + g] = __ldg(&arena.cellTris[cellFirst + k]);
-                        nh++;
-                    }
-                p.diagCar[2 * p.carStride + g] = nh;
-                for (int r = nh; r < MAX_CAR_TRI_PAIRS; r++) p.diagCar[(3 + r) * p.carStride + g] = -1;
-            }
-
-            if (!cars.n(C_DEMOED, i))
-            {
-                Body body = loadCarBody(cars, i);
-                Susp su = loadSusp(cars, i);
-                float lat[NUM_WHEELS], lon[NUM_WHEELS];
-                #pragma unroll
-                for (int w = 0; w < NUM_WHEELS; w++)
-                {
-                    lat[w] = cars.f(C_LAT + w, i);
-                    lon[w] = cars.f(C_LON + w, i);
-                }
-                applySuspension(body, su, lat, lon, rayDist, rayNormal, cars.n(C_MAN_COUNT, i),
-                                cars.v(C_MAN_N0, i), tick, (p.compatFlags & 1) != 0);
-
-                MPoint pts[MAX_CAR_MANIFOLD_POINTS];
-                int count = planeManifold(cen, rot, pts);
-                const int planeCount = count;
-
-                // Best mesh contact over the first MAX_CAR_TRI_PAIRS SAT hits.
-                Contact best{};
-                float bestDist = 3.402823466e+38f;
-                int bestTri = -1;
-                int seen = 0;
-                for (int h = 0; h < L.HW && seen < MAX_CAR_TRI_PAIRS; h++)
-                {
-                    for (unsigned m = hitS[h * L.TC + i]; m && seen < MAX_CAR_TRI_PAIRS; m &= m - 1)
-                    {
-                        seen++;
-                        const int k = h * 32 + __ffs(m) - 1;
-                        const int tri = __ldg(&arena.cellTris[cellFirst + k]);
-                        V3 v0, v1, v2;
-                        int flags;
-                        loadTri(arena, tri, v0, v1, v2, flags);
-                        const LocalTri lt = localTriangle(cen, rot, v0, v1, v2);
-                        const Sat sat = carTriSat(lt);
-                        pairContacts(lt, sat, [&](const Contact& c) {
-                            if (nearManifoldPoint(pts, planeCount, c.carPos)) return;
-                            const float d = -c.depth;
-                            if (d < bestDist)
-                            {
-                                bestDist = d;
-                                best = c;
-                                bestTri = tri;
-                            }
-                        });
-                    }
-                }
-                if (bestTri >= 0)
-                {
-                    V3 v0, v1, v2;
-                    int flags;
-                    loadTri(arena, bestTri, v0, v1, v2, flags);
-                    adjustInternalEdge(localTriangle(cen, rot, v0, v1, v2), triAngles(arena, bestTri), best);
-                    addManifoldPoint(pts, count, contactToManifold(best, cen, rot));
-                }
-
-                if (count > 0)
-                {
-                    solveCarManifold(body, pts, count);
-                    integrateSplitCorrection(body);
-                }
-                cars.n(C_MAN_COUNT, i) = count;
-                cars.setv(C_MAN_N0, i, count > 0 ? pts[0].worldNormal : v3zero());
-                body.vel = body.vel + body.extVel + body.deltaVel;
-                body.ang = body.ang + body.extAng + body.deltaAng;
-                storeCarBody(cars, i, body);
-                storeSusp(cars, i, su);
-                #pragma unroll
-                for (int w = 0; w < NUM_WHEELS; w++)
-                {
-                    cars.f(C_LAT + w, i) = lat[w];
-                    cars.f(C_LON + w, i) = lon[w];
-                }
-            }
-        }
-        if (tid == 0) wsumS[0] = 0;  // car-car work counter (the scan's sums are dead here)
-        __syncthreads();
-
-        // ---- car-car pairs: one thread per sim that has a pair within reach ----
-        // Sims are independent, so the compacted order does not affect results;
-        // within a sim the pairs run in the reference's order (a < b).
-        {
-            int* activeS = cntS;  // per-car counts are dead until the next tick
-            int& nActive = wsumS[0];
-            const int nPairs = nCars * (nCars - 1) / 2;
-            if (tid < simsHere)
-            {
-                const int sb = tid * nCars;
-                bool gate = false;
-                for (int a = 0; a < nCars - 1 && !gate; a++)
-                    for (int b = a + 1; b < nCars && !gate; b++) gate = carCarGate(cars, sb + b, sb + a);
-                if (gate) activeS[atomicAdd(&nActive, 1)] = tid;
-                else if (lastTick && p.diagSim)
-                    for (int q = 0; q < nPairs && q < DIAG_SIM_WORDS; q++) p.diagSim[q * p.simStride + simBase + tid] = 0;
-            }
-            __syncthreads();
-            for (int j = tid; j < nActive; j += blockDim.x)
-            {
-                const int sIdx = activeS[j];
-                const int sb = sIdx * nCars;
-                SimCars<SmemSoa> sc{ cars, sb, nCars, p.nBlue, (int)(p.globalCarBase + carBase + sb), tick, p.seed };
-                int pair = 0;
-                for (int a = 0; a < nCars - 1; a++)
-                    for (int b = a + 1; b < nCars; b++, pair++)
-                    {
-                        const int kept = solveCarCarPair(sc, b, a);
-                        if (lastTick && p.diagSim && pair < DIAG_SIM_WORDS)
-                            p.diagSim[pair * p.simStride + simBase + sIdx] = kept;
-                    }
-            }
-        }
-        __syncthreads();
-
-        // ---- ball: arena contacts (one warp per sim), then cars + integration (one thread per sim) ----
-        for (int s = warp; s < simsHere; s += L.W)
-            ballArenaStage(cars, sims, s, nCars, tick, arena, wbuf, lane, rsS, L.TS);
-        __syncthreads();
-        if (tid < simsHere) ballFinishStage(cars, sims, tid, nCars, tick, rsS, L.TS);
-        __syncthreads();
-
-        // ---- per car: integrate, finish tick; per sim: finish ball ----
-        if (carThread)
-        {
-            const int i = tid;
-            if (!cars.n(C_DEMOED, i))
-            {
-                V3 pos = cars.v(C_POS, i), cen, vel = cars.v(C_VEL, i), ang = cars.v(C_ANG, i);
-                Q4 rot = cars.q(C_ROT, i);
-                integratePose(pos, cen, rot, vel, ang);
-                clampCarVelocity(vel, ang);
-                cars.setv(C_POS, i, pos);
-                cars.setv(C_VEL, i, vel);
-                cars.setv(C_ANG, i, ang);
-                cars.setv(C_CEN, i, cen);
-                cars.setq(C_ROT, i, rot);
-            }
-            if (finishCar(cars, i, ctl.steer, myLocal >= p.nBlue, c_tables)) respawned = true;
-        }
-        if (tid < simsHere) finishBall(sims, tid);
-        __syncthreads();
-
-        // ---- boost pads ----
-        // Pad-major item order: a warp's lanes share a pad, so the pad table
-        // reads from constant memory are warp-uniform.  Pads never overlap, so
-        // no car can be claimed by two pads in the same tick.
-        for (int it = tid; it < simsHere * NUM_BOOST_PADS; it += blockDim.x)
-        {
-            const int pad = it / simsHere;
-            const int s = it - pad * simsHere;
-            boostPad(cars, s * nCars, nCars, sims, s, pad, c_tables);
-        }
-        __syncthreads();
-
-        if (lastTick && carThread)
-        {
-            const long long g = carBase + tid;
-            int* outI = reinterpret_cast<int*>(p.carOut);
-            #pragma unroll
-            for (int w = 0; w < NUM_WHEELS; w++)
-                outI[(long long)(O_WHEEL_CON + w) * p.carStride + g] = respawned ? 0 : (int)((wheelContactBits >> w) & 1u);
-        }
-        respawned = false;
-    }
-
-    // ---- store the tile ----
-    if (carThread)
-    {
-        const long long g = carBase + tid;
-        p.carOut[(long long)(O_CONTROLS + 0) * p.carStride + g] = ctl.throttle;
-        p.carOut[(long long)(O_CONTROLS + 1) * p.carStride + g] = ctl.steer;
-        p.carOut[(long long)(O_CONTROLS + 2) * p.carStride + g] = ctl.yaw;
-        p.carOut[(long long)(O_CONTROLS + 3) * p.carStride + g] = ctl.pitch;
-        p.carOut[(long long)(O_CONTROLS + 4) * p.carStride + g] = ctl.roll;
-        int* outI = reinterpret_cast<int*>(p.carOut);
-        outI[(long long)(O_CONTROLS + 5) * p.carStride + g] = ctl.jump;
-        outI[(long long)(O_CONTROLS + 6) * p.carStride + g] = ctl.boost;
-        outI[(long long)(O_CONTROLS + 7) * p.carStride + g] = ctl.slide;
-    }
-    for (int w = 0; w < NCW; w++)
-        for (int i = tid; i < carsHere; i += blockDim.x)
-            p.car[(long long)w * p.carStride + carBase + i] = cars.f(w, i);
-    for (int w = 0; w < NSW; w++)
-        for (int i = tid; i < simsHere; i += blockDim.x)
-            p.sim[(long long)w * p.simStride + simBase + i] = sims.f(w, i);
-}
-
-
 // =========================================================================================
-// Staged path: the same tick as a sequence of kernels over the state in global memory
-// (resident in L2 between stages), so each stage runs at its own occupancy and no warp
-// waits on a CTA barrier for unrelated work.  Per tick:
+// Stage kernels, per tick and sim slice:
 //   flatKernel     begin step, broadphase, (car, candidate) wheel rays + SAT, per CTA of cars
 //   rayCtlKernel   ray finish (arena hit, other cars' boxes, ball), controls
 //   suspKernel     suspension; cars that may touch a plane or the mesh are listed
@@ -1461,7 +852,7 @@ __global__ void __launch_bounds__(SOLVE_BLOCK) suspKernel(TickParams p, ArenaDev
         lon[w] = cars.f(C_LON + w, i);
     }
     applySuspension(body, su, lat, lon, rayDist, rayNormal, cars.n(C_MAN_COUNT, i), cars.v(C_MAN_N0, i), tick,
-                    (p.compatFlags & 1) != 0);
+                    (p.compatFlags & CARLB_SOURCE_LAGGED_LATERAL_FRICTION) == 0);
     storeSusp(cars, i, su);
     #pragma unroll
     for (int w = 0; w < NUM_WHEELS; w++)
@@ -1649,7 +1040,7 @@ __global__ void __launch_bounds__(SOLVE_BLOCK) contactKernel(TickParams p, Arena
     }
 }
 
-__global__ void __launch_bounds__(CC_BLOCK) carCarKernel(TickParams p, int t)
+__global__ void __launch_bounds__(CC_BLOCK) carCarKernel(TickParams p, StageScratch x, int t)
 {
     __shared__ int activeS[CC_BLOCK];
     __shared__ int nActive;
@@ -1673,6 +1064,7 @@ __global__ void __launch_bounds__(CC_BLOCK) carCarKernel(TickParams p, int t)
             for (int q = 0; q < nPairs && q < DIAG_SIM_WORDS; q++) p.diagSim[q * p.simStride + s] = 0;
     }
     __syncthreads();
+    if (tid == 0 && nActive) atomicAdd(x.ccCount, nActive);
     // The active sims are packed into the first lanes; those lanes of each warp
     // step their sims together.
     const unsigned lanes = __ballot_sync(FULL, tid < nActive);
@@ -1738,8 +1130,13 @@ __global__ void __launch_bounds__(FIN_THREADS) finishKernel(TickParams p, StageS
 
     if (blockIdx.x == 0 && tid == 0)
     {
-        // The per-tick work lists are consumed; empty them for the next tick.
+        // The per-tick work lists are consumed; keep their sizes and empty them
+        // for the next tick.
+        for (int c = 0; c < HEAVY_CLASSES; c++) x.stats[c] = x.heavyCount[c];
+        x.stats[HEAVY_CLASSES] = *x.ballCount;
+        x.stats[HEAVY_CLASSES + 1] = *x.ccCount;
         *x.ballCount = 0;
+        *x.ccCount = 0;
         for (int c = 0; c < HEAVY_CLASSES; c++) x.heavyCount[c] = 0;
     }
     if (tid < simsHere) ballFinishStage(cars, sims, s0 + tid, nCars, tick, x.ball, (int)p.simStride);
@@ -1795,39 +1192,6 @@ int uploadTickTables(const Tables& t)
     return (int)cudaMemcpyToSymbol(c_tables, &t, sizeof(Tables));
 }
 
-int tickThreads(int tileSims, int nCars)
-{
-    const int cars = tileSims * nCars;
-    return ((cars + 31) / 32) * 32;
-}
-
-size_t tickSmemBytes(int tileSims, int nCars, int hitWords, int threads)
-{
-    return (size_t)layoutOf(tileSims, nCars, hitWords, threads).total * 4;
-}
-
-int launchTick(const TickParams& p, const ArenaDev& a, void* stream)
-{
-    if (p.nTicks <= 0 || p.nSim <= 0) return 0;
-    const int threads = tickThreads(p.tileSims, p.nCars);
-    const size_t smem = tickSmemBytes(p.tileSims, p.nCars, a.hitWords, threads);
-    // The shared-memory opt-in is a per-device function attribute.
-    static bool configured[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64 || !configured[dev])
-    {
-        const cudaError_t err = cudaFuncSetAttribute(tickKernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                     227 * 1024);
-        if (err != cudaSuccess) return (int)err;
-        if (dev >= 0 && dev < 64) configured[dev] = true;
-    }
-    const int blocks = (p.nSim + p.tileSims - 1) / p.tileSims;
-    tickKernel<<<blocks, threads, smem, (cudaStream_t)stream>>>(p, a);
-    return (int)cudaGetLastError();
-}
-
-
 // ---- fixed-size scratch for carlb_ticks_static_scratch --------------------------------------
 // A file-scope device array, so that entry point allocates nothing at call time
 // (for callers that cannot call cudaMalloc while stepping).  Every GPU that loads
@@ -1837,10 +1201,13 @@ int launchTick(const TickParams& p, const ArenaDev& a, void* stream)
 // share it and race.
 static __device__ __align__(256) unsigned char g_staticScratch[STATIC_SCRATCH_BYTES];
 
-int staticScratchAddress(void** ptr, size_t* bytes)
+int stagedSetup();
+
+int staticScratchAddress(void** ptr, size_t* bytes, void** lastUse)
 {
     static std::mutex lock;
     static void* cached[64] = {};
+    static cudaEvent_t used[64] = {};
     int dev = 0;
     cudaError_t err = cudaGetDevice(&dev);
     if (err != cudaSuccess) return (int)err;
@@ -1848,6 +1215,22 @@ int staticScratchAddress(void** ptr, size_t* bytes)
     std::lock_guard<std::mutex> guard(lock);
     if (!cached[dev])
     {
+        // Load every kernel the static-scratch ticks launch, and set the flat
+        // stage's shared-memory opt-in, now: with lazy module loading a kernel's
+        // first launch would otherwise load its code and may allocate device
+        // memory inside a call that promises to allocate nothing.
+        const void* kernels[] = { (const void*)ballPrepKernel, (const void*)flatKernel, (const void*)rayCtlKernel,
+                                  (const void*)suspKernel, (const void*)contactKernel, (const void*)carCarKernel,
+                                  (const void*)ballKernel, (const void*)finishKernel };
+        for (const void* k : kernels)
+        {
+            cudaFuncAttributes attr;
+            err = cudaFuncGetAttributes(&attr, k);
+            if (err != cudaSuccess) return (int)err;
+        }
+        if (const int e = stagedSetup()) return e;
+        err = cudaEventCreateWithFlags(&used[dev], cudaEventDisableTiming);
+        if (err != cudaSuccess) return (int)err;
         void* p = nullptr;
         err = cudaGetSymbolAddress(&p, g_staticScratch);
         if (err != cudaSuccess) return (int)err;
@@ -1856,6 +1239,7 @@ int staticScratchAddress(void** ptr, size_t* bytes)
     }
     *ptr = cached[dev];
     *bytes = STATIC_SCRATCH_BYTES;
+    if (lastUse) *lastUse = used[dev];
     return 0;
 }
 
@@ -1947,6 +1331,8 @@ int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch&
         y.ball = x.ball + s0;
         y.ballList = x.ballList + s0;
         y.ballCount = x.ballCount + g;
+        y.ccCount = x.ccCount + g;
+        y.stats = x.stats + g * STAGE_WORK;
         gp[nG] = q;
         gx[nG] = y;
         gs[nG] = groups == 1 ? st : (cudaStream_t)aux.streams[g];
@@ -2031,7 +1417,7 @@ int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch&
             contactKernel<<<contactBlocks + meshBlocks, SOLVE_BLOCK, 0, sq>>>(q, a, y, t, contactBlocks);
             mark(4, true, sq);
             mark(5, false, sq);
-            carCarKernel<<<(q.nSim + CC_BLOCK - 1) / CC_BLOCK, CC_BLOCK, 0, sq>>>(q, t);
+            carCarKernel<<<(q.nSim + CC_BLOCK - 1) / CC_BLOCK, CC_BLOCK, 0, sq>>>(q, y, t);
             mark(5, true, sq);
             if (sb != sq && (err = cudaStreamWaitEvent(sq, (cudaEvent_t)aux.ballDone[g], 0)) != cudaSuccess)
                 return (int)err;

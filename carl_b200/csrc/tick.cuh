@@ -1,4 +1,4 @@
-// Launch-side description of the fused tick kernel and the device arena.
+// Launch-side description of the stage kernels of the tick and the device arena.
 #pragma once
 
 #include <cstdint>
@@ -53,7 +53,6 @@ struct TickParams
     const int* tickDev;     // staged path: when set, the tick count is read from here instead
                             // (lets a captured graph of the launch be replayed at any tick)
     int nTicks;
-    int tileSims;           // sims per CTA
     int compatFlags;        // carlb_config::compat_flags
 };
 
@@ -73,21 +72,20 @@ struct StageScratch
     float* ball;            // [15][simStride] ball stage hand-over values
     int* ballList;          // [simStride] sims whose ball is moving (arena work), this tick
     int* ballCount;         // [slices] entries of each slice's ballList; zero between ticks
+    int* ccCount;           // [slices] sims whose car-car stage had a pair in reach; zero between ticks
+    int* stats;             // [slices][STAGE_WORK] the last tick's work-list sizes (see STAGE_WORK)
 };
 
 struct Tables;
 // Copies the game tables into this kernel's constant memory.
 int uploadTickTables(const Tables& t);
 
-// Shared-memory bytes of one CTA of the tick kernel.
-size_t tickSmemBytes(int tileSims, int nCars, int hitWords, int threads);
-int tickThreads(int tileSims, int nCars);
-
-// Launches ceil(nSim / tileSims) CTAs on `stream`.
-int launchTick(const TickParams& p, const ArenaDev& a, void* stream);
-
 // Contact work lists: cars with plane contacts only, cars with SAT hits.
 constexpr int HEAVY_CLASSES = 2;
+// Work-list sizes kept per slice for the last tick (carlb_stage_work): cars listed
+// for the contact stage with plane contacts only, cars listed with SAT hits,
+// moving balls listed for the ball stage, sims with a car-car pair in reach.
+constexpr int STAGE_WORK = 4;
 
 // Stage kernels of one tick of the staged path, in launch order:
 // ballPrep, flat, rayCtl, susp, contact, carCar, ball, finish.
@@ -123,8 +121,13 @@ inline void stageSlice(int nSim, int groups, int g, int* s0, int* ns)
 
 // Capacity of the file-scope device scratch used by carlb_ticks_static_scratch.
 constexpr size_t STATIC_SCRATCH_BYTES = 64ull << 20;
-// Device address of that scratch on the current device (looked up once per device).
-int staticScratchAddress(void** ptr, size_t* bytes);
+// Device address of that scratch on the current device, and an event
+// (cudaEvent_t) that marks the end of the last work enqueued on it, so that
+// calls from different envs and streams are ordered on the device.  The first
+// call on a device looks the address up, creates the event and loads every
+// stage kernel the static-scratch ticks launch; carlb_create makes that call,
+// so the ticks themselves allocate nothing.
+int staticScratchAddress(void** ptr, size_t* bytes, void** lastUse);
 
 // One-time per-device setup of the staged kernels (shared-memory opt-in); call
 // before capturing a launch into a graph.

@@ -53,18 +53,21 @@ typedef struct carlb_config {
     int32_t normalize;          /* bool */
     int32_t previous_controls;  /* bool */
     int32_t device;             /* CUDA device ordinal */
-    int32_t compat_flags;       /* CARLB_COMPAT_* bits, 0 = the reference's source semantics */
+    int32_t compat_flags;       /* CARLB_SOURCE_* bits; 0 = what the reference's CUDA build computes */
     int64_t sim_offset;         /* global index of this env's sim 0 (sharding) */
 } carlb_config;
 
-/* compat_flags bits.
- * CARLB_COMPAT_UNLAGGED_LATERAL_FRICTION: use the current tick's lateral wheel
- * friction coefficient instead of the previous tick's.  The reference's source
- * consumes the previous tick's (include/Physics/CarSuspension.cuh:206-209), but
- * it reads that value with __ldg and stores the new one in the same thread, and
- * its sm_100a build (nvcc 12.9, -O3) orders the load after the store.  Setting
- * this bit reproduces that build bit for bit; the default follows the source. */
-#define CARLB_COMPAT_UNLAGGED_LATERAL_FRICTION 1
+/* compat_flags bits.  With no bit set (the default) the tick reproduces what the
+ * reference's sm_100a CUDA build computes, which is what the parity tests hold to
+ * bit-exact candidate lists and SAT pair sets and the 1e-4 / 1e-3 state tolerance.
+ * CARLB_SOURCE_LAGGED_LATERAL_FRICTION: use the previous tick's lateral wheel
+ * friction coefficient, as the reference's source intends
+ * (include/Physics/CarSuspension.cuh:206-209).  Its CUDA build reads that value
+ * with __ldg in the thread that also stores the new one, and nvcc 12.9 (-O3,
+ * sm_100a) orders the load after the store, so the build consumes the current
+ * tick's coefficient; the reference compiled for a host CPU follows the source.
+ * Any other bit is rejected with CARLB_ERR_VALUE. */
+#define CARLB_SOURCE_LAGGED_LATERAL_FRICTION 1
 
 /* Action encodings (one record of 7 values per car, [n_sim, n_cars, 7]). */
 typedef enum carlb_action_kind {
@@ -236,14 +239,19 @@ carlb_status carlb_ticks_host(carlb_env* env, carlb_action_kind kind, const void
  * cudaMalloc can fail.  This call allocates nothing (no cudaMalloc, cudaFree or
  * allocating library routine): the stage scratch comes from a fixed 64 MiB
  * file-scope device array, which every GPU that loads this library holds until
- * the process exits.  Its address is looked up on the first call on each
- * device, so make that first call before capturing any stream.  An env that
- * needs more than 64 MiB of stage scratch (roughly 224 bytes per car and 64 per
- * sim: about 47,000 sims at 3v3) gets CARLB_ERR_VALUE; the fused tick path gets
- * CARLB_ERR_STATE.  Every call shares the array, which keeps the last call's
- * contents (the work-list counters are cleared on each call), so calls that
- * overlap on the GPU (any env, any stream) race: serialise them.  No counterpart
- * in the reference. */
+ * the process exits.  carlb_create does the set-up once per device: it looks up
+ * the array's device address and loads every stage kernel this call launches,
+ * so that even the first call loads no code under lazy module loading.  An env
+ * that needs more than 64 MiB of stage scratch (roughly 224 bytes per car and
+ * 64 per sim: about 47,000 sims at 3v3) gets CARLB_ERR_VALUE before anything is
+ * enqueued.  Every call shares the array, which keeps the last call's contents
+ * (the work-list counters are cleared on each call).  Calls that overlapped on
+ * the GPU would race on it, so each call's work waits on the device for the
+ * previous call's work (any env, any stream) before it touches the array: calls
+ * run one after another on the GPU even when their streams are independent.
+ * The caller's current device is the same on return.  No per-stage timing is recorded
+ * (carlb_stage_times then reports CARLB_ERR_STATE).  No counterpart in the
+ * reference. */
 carlb_status carlb_ticks_static_scratch(carlb_env* env, carlb_action_kind kind, const void* actions,
                                         int32_t n_ticks);
 carlb_status carlb_reset(carlb_env* env);
@@ -308,6 +316,14 @@ carlb_status carlb_set_stage_timing(carlb_env* env, int32_t enabled);
  * ball prelude, candidates (flat), ray finish + controls, suspension, contact
  * solve, car-car, ball arena, finish.  Waits for that tick to complete. */
 carlb_status carlb_stage_times(carlb_env* env, float* ms, int32_t capacity, int32_t* count);
+
+/* Work-list sizes of the last tick of the last carlb_ticks / carlb_env_step call,
+ * summed over the sim slices: [0] cars listed for the contact stage with plane
+ * contacts only, [1] cars listed with SAT hits, [2] moving balls listed for the
+ * ball stage, [3] sims with a car-car pair in reach.  Waits for the env stream.
+ * A measurement aid (the list-driven stages' byte models); no counterpart in
+ * the reference. */
+carlb_status carlb_stage_work(carlb_env* env, int32_t counts[4]);
 
 /* Action mask of observation rows, on the device: obs is float32 [rows, obs_dim]
  * (device memory, row-major), mask receives uint8 [rows, 18] (1 = logit allowed),

@@ -1,10 +1,10 @@
 """Shared pytest configuration.
 
 Markers:
-  gpu   needs a CUDA device (runs the fused tick kernel); everything else runs
-        on CPU and covers the oracle, the host build of the product physics,
-        the arena build, the C ABI library's exports and the multi-process host
-        logic.
+  gpu   needs a CUDA device (runs the staged sm_100a tick kernels and the env
+        kernels); everything else runs on CPU and covers the oracle, the host
+        build of the product physics, the arena build, the C ABI library's
+        exports and the multi-process host logic.
 """
 
 from __future__ import annotations
@@ -22,7 +22,9 @@ for p in (str(ROOT), str(TESTS)):
     if p not in sys.path:
         sys.path.insert(0, p)
 
-REFERENCE = Path("/root/reference")
+from oracle import paths as _oracle_paths  # noqa: E402
+
+REFERENCE = _oracle_paths.reference_dir()
 
 
 def pytest_configure(config):
@@ -53,7 +55,7 @@ def oracle_built() -> Path:
     ref = ROOT / "oracle" / "_ref"
     need = [ref / "libcarlref_cpu.so", ref / "libcarlref_ka.so", ref / "arena.obj"]
     if not all(p.exists() for p in need):
-        if not REFERENCE.exists():
+        if not _oracle_paths.reference_present():
             pytest.skip("oracle not built and the reference tree is absent")
         subprocess.run(["make", "-C", str(ROOT / "oracle"), "cpu", "arena"], check=True, capture_output=True)
     os.environ.setdefault("CARL_ARENA_OBJ", str(ref / "arena.obj"))

@@ -49,15 +49,30 @@ def compare_field(name: str, a: np.ndarray, b: np.ndarray) -> dict:
             "max_abs": err}
 
 
+SAT_CAP = 32  # pair slots per car (include/RLConstants.cuh MAX_CAR_TRI_PAIRS)
+
+
 def compare_sat_pairs(a: np.ndarray, b: np.ndarray) -> np.ndarray:
-    """Rows whose SAT pair sets differ (order within a row is free)."""
+    """Rows whose SAT pair sets differ (order within a row is free).
+
+    Word 0 of a row is the hit count (at most SAT_CAP), the rest the triangle
+    ids.  A car with SAT_CAP or more hits keeps, in the reference's CUDA build,
+    the pairs that won its atomicAdd slots (include/Physics/CarArena/
+    SAT.cuh:149-150), so for full rows only the counts are compared."""
     ia, ib = a.view(np.int32), b.view(np.int32)
-    bad = []
-    for r in range(ia.shape[0]):
-        na, nb = ia[r, 0], ib[r, 0]
-        if na != nb or set(ia[r, 1:1 + na].tolist()) != set(ib[r, 1:1 + nb].tolist()):
-            bad.append(r)
-    return np.array(bad, dtype=np.int64)
+    na, nb = ia[:, 0], ib[:, 0]
+    bad = na != nb
+    width = ia.shape[1] - 1
+    k = np.minimum(np.minimum(na, nb), width)
+    cols = np.arange(width)[None, :]
+    valid = cols < k[:, None]
+    big = np.iinfo(np.int32).max
+    sa = np.sort(np.where(valid, ia[:, 1:], big), axis=1)
+    sb = np.sort(np.where(valid, ib[:, 1:], big), axis=1)
+    sets_differ = (sa != sb).any(axis=1)
+    capped = (na >= SAT_CAP) & (nb >= SAT_CAP)
+    bad |= sets_differ & ~capped
+    return np.where(bad)[0].astype(np.int64)
 
 
 # The ball's cached integration state is dead while BALL_INT_VALID is 0 (the
@@ -81,9 +96,27 @@ def _mask_dead_ball_cache(a: dict, b: dict) -> tuple[dict, dict]:
     return a, b
 
 
+def _mask_dead_manifold_normal(a: dict, b: dict) -> tuple[dict, dict]:
+    """The manifold's first world normal is read only while the car's manifold
+    count is non-zero (include/Physics/CarSuspension.cuh:234-265); resets set
+    the count to 0 and leave the normal, which the reference's CUDA build
+    allocates without clearing (include/Cuda/DeviceArray.cuh:8-12)."""
+    if "MAN_COUNT" not in a or "MAN_COUNT" not in b or "MAN_NORMAL0" not in a or "MAN_NORMAL0" not in b:
+        return a, b
+    dead = (a["MAN_COUNT"][:, 0] == 0) & (b["MAN_COUNT"][:, 0] == 0)
+    if not dead.any():
+        return a, b
+    a, b = dict(a), dict(b)
+    a["MAN_NORMAL0"], b["MAN_NORMAL0"] = a["MAN_NORMAL0"].copy(), b["MAN_NORMAL0"].copy()
+    a["MAN_NORMAL0"][dead] = 0
+    b["MAN_NORMAL0"][dead] = 0
+    return a, b
+
+
 def compare_snapshots(a: dict, b: dict, fields=None) -> dict:
     fields = fields or [f for f in a if f in b]
     a, b = _mask_dead_ball_cache(a, b)
+    a, b = _mask_dead_manifold_normal(a, b)
     return {name: compare_field(name, a[name], b[name]) for name in fields}
 
 

@@ -119,5 +119,5 @@ def test_field_and_buffer_enums_match_the_header():
     assert [n for n, _ in sorted(fields, key=lambda x: int(x[1]))] == capi.FIELDS
     bufs = [b for b in re.findall(r"\bCARLB_BUF_([A-Z_]+)\s*=\s*(\d+)", text) if b[0] != "COUNT"]
     assert len(bufs) == 12 and sorted(int(v) for _, v in bufs) == list(range(12))
-    assert re.search(r"CARLB_COMPAT_UNLAGGED_LATERAL_FRICTION\s+(\d+)", text).group(1) == str(
-        capi.COMPAT_UNLAGGED_LATERAL_FRICTION)
+    assert re.search(r"CARLB_SOURCE_LAGGED_LATERAL_FRICTION\s+(\d+)", text).group(1) == str(
+        capi.SOURCE_LAGGED_LATERAL_FRICTION)

@@ -12,7 +12,9 @@ import pytest
 import carl_b200
 from carl_b200 import carl as front
 
-REFERENCE = Path("/root/reference")
+from oracle.paths import reference_dir
+
+REFERENCE = reference_dir()
 
 
 def test_constants_match_the_reference_module():

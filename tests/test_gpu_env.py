@@ -46,6 +46,7 @@ def buffers_close(ours: np.ndarray, theirs: np.ndarray) -> int:
     return int((ours != theirs.astype(ours.dtype)).sum())
 
 
+@pytest.mark.parametrize("oracle", ["cuda_build", "host_build"])
 @pytest.mark.parametrize("nb, no, kind, frameskip, flags", [
     (2, 2, capi.ACTIONS_DISCRETE, 8, {}),
     (2, 2, capi.ACTIONS_CONTINUOUS, 8, {}),
@@ -53,14 +54,17 @@ def buffers_close(ours: np.ndarray, theirs: np.ndarray) -> int:
     (1, 1, capi.ACTIONS_DISCRETE, 2, {"normalize": True}),
     (1, 2, capi.ACTIONS_DISCRETE, 1, {"previous_controls": True, "invert_orange": False}),
 ])
-def test_env_step_matches_reference(oracle_built, nb, no, kind, frameskip, flags):
-    from oracle.refenv import RefCpu
+def test_env_step_matches_reference(oracle_built, nb, no, kind, frameskip, flags, oracle):
+    """Env steps in the default mode against the reference's CUDA build, and in
+    the source-semantics mode against the reference's host build."""
+    from oracle.refenv import RefCpu, RefGpu
 
     n_sim, seed = 64, 11 + nb + 3 * no
     rng = np.random.default_rng(seed)
     n = n_sim * (nb + no)
-    env = capi.Env(n_sim, nb, no, seed, frameskip=frameskip, **flags)
-    ref = RefCpu(n_sim, nb, no, seed, frameskip=frameskip, **flags)
+    compat = 0 if oracle == "cuda_build" else capi.SOURCE_LAGGED_LATERAL_FRICTION
+    env = capi.Env(n_sim, nb, no, seed, frameskip=frameskip, compat_flags=compat, **flags)
+    ref = (RefGpu if oracle == "cuda_build" else RefCpu)(n_sim, nb, no, seed, frameskip=frameskip, **flags)
     env.set_limit(capi.LIMIT_MAX_TICKS, 300)
     env.set_limit(capi.LIMIT_NO_TOUCH_TIMEOUT_TICKS, 200)
     ref.set_limits(300, -1, 200, -1)
@@ -85,7 +89,8 @@ def test_env_step_matches_reference(oracle_built, nb, no, kind, frameskip, flags
 def test_env_step_golden():
     z = np.load(GOLDEN / "env_step_1v1.npz")
     n_sim, nb, no, seed, frameskip = (int(x) for x in z["dims"])
-    env = capi.Env(n_sim, nb, no, seed, frameskip=frameskip)
+    # The golden vectors come from the reference's host build (source semantics).
+    env = capi.Env(n_sim, nb, no, seed, frameskip=frameskip, compat_flags=capi.SOURCE_LAGGED_LATERAL_FRICTION)
     env.reset()
     names = {"obs": capi.BUF_OBS, "state": capi.BUF_STATE, "rewards": capi.BUF_REWARDS, "dones": capi.BUF_DONES,
              "episode_ticks": capi.BUF_EPISODE_TICKS, "transition_obs": capi.BUF_TRANSITION_OBS}
@@ -177,7 +182,7 @@ def test_apply_reset_state_matches_reference_cuda_build(oracle_built, mode):
     n_sim, nb, no, seed = 48, 2, 2, 6
     n_cars = nb + no
     rng = np.random.default_rng(17)
-    env = capi.Env(n_sim, nb, no, seed, compat_flags=capi.COMPAT_UNLAGGED_LATERAL_FRICTION)
+    env = capi.Env(n_sim, nb, no, seed)
     ref = RefGpu(n_sim, nb, no, seed)
     env.reset()
     ref.reset()

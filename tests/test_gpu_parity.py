@@ -1,20 +1,26 @@
-"""Parity of the fused sm_100a tick kernel with the reference.
+"""Parity of the sm_100a staged tick with the reference.
 
 Two oracles (both built from the reference's own sources):
-  * RefGpu: the reference's CUDA build for sm_100a.  With
-    COMPAT_UNLAGGED_LATERAL_FRICTION the product reproduces what that build
-    computes (its compiled code reads the lateral friction coefficient after
-    the current tick's store; the source intends the previous tick's value).
+  * RefGpu: the reference's CUDA build for sm_100a.  The product's default mode
+    (compat_flags = 0) reproduces what that build computes, including its
+    compiled read of the current tick's lateral friction coefficient (the
+    source intends the previous tick's value).  This is the mode the benchmark
+    runs, and it is held to the strict gates below at small sizes and at the
+    benchmark's full size.
   * RefCpu: the reference's tick compiled for the host, which follows the
-    source semantics.  The product's default mode follows the same semantics;
-    the remaining differences come from device intrinsics (rsqrtf, __sincosf)
-    that the reference's own CUDA build has too.
+    source semantics.  The product's SOURCE_LAGGED_LATERAL_FRICTION mode follows
+    the same semantics; the remaining differences come from device intrinsics
+    (rsqrtf, __sincosf) that the reference's own CUDA build has too.
 
-Tolerances (the parity contract): candidate lists and SAT pair sets bit-exact;
-single-tick fp32 state within 1e-4 relative or 1e-3 absolute; integer words
-exact.  8-tick rollouts: a stated drift bound on the rows that leave that
-tolerance (contacts are chaotic: one ulp in a contact normal can flip a
-discrete event such as a wheel touching down).
+Gates of the default mode against RefGpu: broadphase cells, candidate counts
+and SAT pair sets bit-exact; single-tick fp32 state within 1e-4 relative or
+1e-3 absolute and integer words exact, for every sim row and every car row
+except cars whose SAT pairs the reference's CUDA build offers to its manifold
+in run-dependent order (it fills the pair slots with atomicAdd,
+include/Physics/CarArena/SAT.cuh:149-150, so of two equally deep mesh contacts
+either may be kept).  8-tick rollouts: a stated drift bound on the car rows
+that leave that tolerance (contacts are chaotic: one ulp in a contact normal
+can flip a discrete event such as a wheel touching down).
 """
 
 from __future__ import annotations
@@ -37,14 +43,18 @@ SCENARIOS = [
 IDS = [s[0] for s in SCENARIOS]
 
 # Share of car rows allowed outside the single-tick tolerance after 8 ticks
-# (the stated drift bound).  Dense car-car play (crowd) amplifies last-ulp
-# differences through discrete contact events; measured: 4v4 crowd 15.6 %,
-# 3v3 crowd about 10 % against the host build.
+# (the stated drift bound).  Default mode against the reference CUDA build:
+# 2 % (measured 0 % on every scenario but 3v3 floor).  Source mode against the
+# host build: dense car-car play (crowd) amplifies last-ulp differences through
+# discrete contact events; measured 4v4 crowd 15.6 %, 3v3 crowd about 10 %.
 DRIFT_ROWS_8 = 0.02
 DRIFT_ROWS_8_CROWD = 0.25
-# Share of car rows allowed outside the single-tick tolerance after one tick
-# against the host build (device rsqrtf/__sincosf versus host libm).
+# SOURCE_LAGGED_LATERAL_FRICTION mode against the host build only (not the
+# benchmarked mode): share of car rows allowed outside the single-tick
+# tolerance (device rsqrtf/__sincosf versus host libm; measured 0 % floor and
+# mixed, 1.0-1.5 % crowd) and share of cars in another broadphase cell.
 SINGLE_TICK_ROWS_HOST = 0.02
+CELLS_HOST = 0.005
 
 
 def _torch():
@@ -95,52 +105,84 @@ def car_rows_bad(rep: dict, n_cars_total: int) -> float:
     return parity.bad_row_fraction(rep, n_cars_total)
 
 
+def check_tick1_against_cuda_build(name, n_sim, n_cars, a, b, diag):
+    """The single-tick gates of the default mode (see the module docstring)."""
+    rows = n_sim * n_cars
+    rep = parity.compare_snapshots(a, b)
+    assert (diag["DIAG_CELL_IDX"][0] == diag["DIAG_CELL_IDX"][1]).all(), f"{name}: broadphase cells differ"
+    assert (diag["DIAG_NUM_TRIS"][0] == diag["DIAG_NUM_TRIS"][1]).all(), f"{name}: candidate counts differ"
+    sat_bad = parity.compare_sat_pairs(*diag["DIAG_SAT_PAIRS"])
+    assert sat_bad.size == 0, f"{name}: SAT pair sets differ on car rows {sat_bad[:10].tolist()}"
+    bad = set()
+    for r in rep.values():
+        if r["rows"] == rows:
+            bad.update(r["bad_rows"].tolist())
+    pairs = diag["DIAG_SAT_PAIRS"][1].view(np.int32)[:, 0]
+    unexplained = sorted(row for row in bad if pairs[row] < 2)
+    assert not unexplained, f"{name} tick 1 car rows {unexplained[:10]}\n" + parity.summarize(rep)
+    # Rows with two or more SAT pairs may keep another, equally deep contact in
+    # the reference; they stay rare (measured 0 or 1 per scenario).
+    assert len(bad) <= max(1, rows // 1000), parity.summarize(rep)
+    sims_ok = {k: r for k, r in rep.items() if r["rows"] == n_sim and n_sim != rows}
+    assert parity.all_ok(sims_ok), parity.summarize(sims_ok)
+    return len(bad)
+
+
 @pytest.mark.parametrize("name, n_sim, nb, no, scenario, seed", SCENARIOS, ids=IDS)
-def test_compat_matches_reference_cuda_build(oracle_built, name, n_sim, nb, no, scenario, seed):
+def test_default_matches_reference_cuda_build(oracle_built, name, n_sim, nb, no, scenario, seed):
     from oracle.refenv import RefGpu
 
     s0 = warm_snapshot(n_sim, nb, no, scenario, seed)
     ctl = workloads.controls(np.random.default_rng(seed + 99), n_sim * (nb + no))
-    results = run_pair(n_sim, nb, no, seed, s0, ctl, capi.COMPAT_UNLAGGED_LATERAL_FRICTION, RefGpu, (1, 8))
+    results = run_pair(n_sim, nb, no, seed, s0, ctl, 0, RefGpu, (1, 8))
     for k, a, b, diag in results:
-        rep = parity.compare_snapshots(a, b)
         if k == 1:
-            # Candidate lists and SAT pair sets: bit-exact.
-            assert (diag["DIAG_CELL_IDX"][0] == diag["DIAG_CELL_IDX"][1]).all()
-            assert (diag["DIAG_NUM_TRIS"][0] == diag["DIAG_NUM_TRIS"][1]).all()
-            assert parity.compare_sat_pairs(*diag["DIAG_SAT_PAIRS"]).size == 0
-            # The reference CUDA build fills its SAT pair slots with atomicAdd, so
-            # the order in which it offers equally deep mesh contacts to the
-            # manifold varies from run to run; a car with two or more SAT pairs
-            # can therefore keep a different (equally deep) contact.  Every other
-            # car must agree within tolerance.
-            bad = set()
-            for r in rep.values():
-                if r["rows"] == n_sim * (nb + no):
-                    bad.update(r["bad_rows"].tolist())
-            pairs = diag["DIAG_SAT_PAIRS"][1].view(np.int32)[:, 0]
-            unexplained = [row for row in bad if pairs[row] < 2]
-            assert not unexplained, f"{name} tick 1 rows {unexplained}\n" + parity.summarize(rep)
-            assert len(bad) <= max(1, n_sim * (nb + no) // 200), parity.summarize(rep)
-            sims_ok = {k2: r for k2, r in rep.items() if r["rows"] == n_sim}
-            assert parity.all_ok(sims_ok), parity.summarize(sims_ok)
+            check_tick1_against_cuda_build(name, n_sim, nb + no, a, b, diag)
         else:
-            frac = car_rows_bad(rep, n_sim * (nb + no))
-            print(f"{name}: compat vs reference CUDA build, 8 ticks: {100 * frac:.2f}% car rows outside tolerance")
-            assert frac <= DRIFT_ROWS_8, parity.summarize(rep)
+            frac = car_rows_bad(parity.compare_snapshots(a, b), n_sim * (nb + no))
+            print(f"{name}: default mode vs reference CUDA build, 8 ticks: {100 * frac:.2f}% car rows outside tolerance")
+            assert frac <= DRIFT_ROWS_8, parity.summarize(parity.compare_snapshots(a, b))
+
+
+def test_bench_size_matches_reference_cuda_build(oracle_built):
+    """The benchmark's workload at its full size: 3v3, n_sim = 32768, the seeded
+    floor states of bench.py (rank 0) after its 5 warm-up steps of 8 ticks, then
+    1 and 8 ticks of the next control set, default mode against the reference's
+    CUDA build on the same states and controls."""
+    from oracle.refenv import RefGpu
+
+    n_sim, nb, no, seed = 32768, 3, 3, 0
+    n = n_sim * (nb + no)
+    ref = RefGpu(n_sim, nb, no, seed)
+    workloads.floor_state(ref, seed)
+    rng = np.random.default_rng(seed + 1)
+    pool = [workloads.controls(rng, n) for _ in range(6)]
+    for i in range(5):
+        ref.ticks(capi.ACTIONS_DIRECT, pool[i], 8)
+    s0 = ref.snapshot()
+    ref.close()
+    results = run_pair(n_sim, nb, no, seed, s0, pool[5], 0, RefGpu, (1, 8))
+    for k, a, b, diag in results:
+        if k == 1:
+            nbad = check_tick1_against_cuda_build("C3 32768", n_sim, nb + no, a, b, diag)
+            print(f"C3 n_sim=32768 tick 1: {nbad} car rows outside tolerance (all with >= 2 SAT pairs)")
+        else:
+            frac = car_rows_bad(parity.compare_snapshots(a, b), n)
+            print(f"C3 n_sim=32768, 8 ticks: {100 * frac:.3f}% car rows outside tolerance")
+            assert frac <= DRIFT_ROWS_8, parity.summarize(parity.compare_snapshots(a, b))
 
 
 @pytest.mark.parametrize("name, n_sim, nb, no, scenario, seed", SCENARIOS, ids=IDS)
-def test_default_matches_reference_semantics(oracle_built, name, n_sim, nb, no, scenario, seed):
-    """Default mode (the source's one-tick-lagged lateral friction) against the
-    reference's host build.  Device intrinsics separate any CUDA build from a
+def test_source_mode_matches_reference_semantics(oracle_built, name, n_sim, nb, no, scenario, seed):
+    """SOURCE_LAGGED_LATERAL_FRICTION mode (the source's one-tick-lagged lateral
+    friction; not the default) against the reference's host build.  Device intrinsics separate any CUDA build from a
     host build by a few ulps; in dense car-car play these can flip a discrete
     contact event within a tick."""
     from oracle.refenv import RefCpu
 
     s0 = warm_snapshot(n_sim, nb, no, scenario, seed)
     ctl = workloads.controls(np.random.default_rng(seed + 77), n_sim * (nb + no))
-    results = run_pair(n_sim, nb, no, seed, s0, ctl, 0, RefCpu, (1, 8))
+    results = run_pair(n_sim, nb, no, seed, s0, ctl, capi.SOURCE_LAGGED_LATERAL_FRICTION, RefCpu, (1, 8))
     n = n_sim * (nb + no)
     for k, a, b, diag in results:
         rep = parity.compare_snapshots(a, b)
@@ -148,7 +190,7 @@ def test_default_matches_reference_semantics(oracle_built, name, n_sim, nb, no, 
         print(f"{name}: tick {k}: {100 * frac:.2f}% car rows outside tolerance of the host build")
         if k == 1:
             cells_diff = (diag["DIAG_CELL_IDX"][0] != diag["DIAG_CELL_IDX"][1]).mean()
-            assert cells_diff <= 0.005
+            assert cells_diff <= CELLS_HOST
             assert frac <= SINGLE_TICK_ROWS_HOST, parity.summarize(rep)
         else:
             bound = DRIFT_ROWS_8_CROWD if scenario == "crowd" else DRIFT_ROWS_8
@@ -157,13 +199,14 @@ def test_default_matches_reference_semantics(oracle_built, name, n_sim, nb, no, 
 
 @pytest.mark.parametrize("case", ["2v2_mixed", "3v3_crowd", "1v1_floor"])
 def test_golden_ticks_on_device(case):
-    """The committed golden vectors (reference host build) reproduced by the
-    kernel within the single-tick tolerance."""
+    """The committed golden vectors (reference host build, source semantics)
+    reproduced by the kernel in SOURCE_LAGGED_LATERAL_FRICTION mode within the
+    single-tick tolerance."""
     from test_golden import load_tick
 
     torch = _torch()
     (n_sim, nb, no, seed), ctl, g = load_tick(case)
-    env = capi.Env(n_sim, nb, no, seed)
+    env = capi.Env(n_sim, nb, no, seed, compat_flags=capi.SOURCE_LAGGED_LATERAL_FRICTION)
     env.set_diagnostics(True)
     env.restore(g["s0"])
     env.ticks(capi.ACTIONS_DIRECT, torch.from_numpy(ctl.view(np.int32)).cuda(), 1)

@@ -109,7 +109,7 @@ def test_native_metadata_matches_reference_cuda_build(metadata, monkeypatch):
     from oracle.refenv import RefGpu
 
     n_sim, nb, no, seed = 512, 1, 1, 11
-    env = capi.Env(n_sim, nb, no, seed, compat_flags=capi.COMPAT_UNLAGGED_LATERAL_FRICTION)
+    env = capi.Env(n_sim, nb, no, seed)
     ref = RefGpu(n_sim, nb, no, seed)
     workloads.mixed_state(env, 12)
     s0 = place_balls(env.snapshot(), n_sim, 13)
@@ -133,10 +133,10 @@ def test_native_metadata_matches_reference_cuda_build(metadata, monkeypatch):
     # The native branch is taken: without the metadata the same 8 ticks differ
     # for the balls that met the arena.
     monkeypatch.delenv("CARL_ARENA_METADATA")
-    plain = capi.Env(n_sim, nb, no, seed, compat_flags=capi.COMPAT_UNLAGGED_LATERAL_FRICTION)
+    plain = capi.Env(n_sim, nb, no, seed)
     plain.restore(s0)
     monkeypatch.setenv("CARL_ARENA_METADATA", str(metadata))
-    native = capi.Env(n_sim, nb, no, seed, compat_flags=capi.COMPAT_UNLAGGED_LATERAL_FRICTION)
+    native = capi.Env(n_sim, nb, no, seed)
     native.restore(s0)
     ctl = torch.from_numpy(workloads.controls(np.random.default_rng(15), n_sim * 2).view(np.int32)).cuda()
     plain.ticks(capi.ACTIONS_DIRECT, ctl, 8)

@@ -76,7 +76,7 @@ def test_sat_pairs_at_the_plane_margin():
     from oracle.refenv import RefGpu
 
     n_sim, nb, no = 2048, 2, 2
-    env = capi.Env(n_sim, nb, no, 7, compat_flags=capi.COMPAT_UNLAGGED_LATERAL_FRICTION)
+    env = capi.Env(n_sim, nb, no, 7)
     _touching_state(env, 8)
     snap = env.snapshot()
     env.set_diagnostics(True)
