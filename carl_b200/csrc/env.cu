@@ -104,6 +104,13 @@ struct carlb_env
     cudaEvent_t stageEv[2 * STAGE_KERNELS] = {};
     bool ballSide = true;  // ball arena stage on a side stream per slice (CARLB_BALL_STREAM=0 disables)
     cudaStream_t ballStream[8] = {};
+    // Arena tables in one allocation with an L2 persisting access-policy window on
+    // the stage kernels (CARLB_L2_WINDOW=1; off by default): the tables' device
+    // pointers and sizes as allocated, then the pool they were moved into.
+    bool l2Window = false;
+    std::vector<std::pair<void**, size_t>> arenaTables;
+    void* arenaPool = nullptr;
+    size_t arenaPoolBytes = 0;
     cudaEvent_t tickStart[8] = {}, ballDone[8] = {};
     bool phaseOffset = true;  // slices alternate their wide stages (CARLB_PHASE_OFFSET=0 disables)
     cudaEvent_t wideDone[8] = {};
@@ -222,6 +229,82 @@ cudaError_t allocZero(carlb_env* e, T** p, size_t count)
     return cudaMemsetAsync(v, 0, count * sizeof(T), e->stream);
 }
 
+// An arena table (read-only after set-up): remembered so that it can be moved
+// into the one pool an L2 access-policy window covers.
+template <class T>
+cudaError_t allocArena(carlb_env* e, T** p, size_t count)
+{
+    const cudaError_t err = allocZero(e, p, count);
+    if (err == cudaSuccess) e->arenaTables.push_back({ reinterpret_cast<void**>(p), count * sizeof(T) });
+    return err;
+}
+
+// Moves the arena tables into one allocation and reserves persisting L2 lines
+// for it (a limit of this process's context; it ends with the process).
+cudaError_t poolArenaTables(carlb_env* e)
+{
+    size_t total = 0;
+    for (const auto& t : e->arenaTables) total += (t.second + 255) & ~(size_t)255;
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    int maxWindow = 0, maxPersist = 0;
+    cudaDeviceGetAttribute(&maxWindow, cudaDevAttrMaxAccessPolicyWindowSize, dev);
+    cudaDeviceGetAttribute(&maxPersist, cudaDevAttrMaxPersistingL2CacheSize, dev);
+    if (total == 0 || (size_t)maxWindow < total || (size_t)maxPersist < total) return cudaSuccess;  // no window
+    err = cudaMalloc(&e->arenaPool, total);
+    if (err != cudaSuccess) return err;
+    e->allocations.push_back(e->arenaPool);
+    size_t off = 0;
+    for (const auto& t : e->arenaTables)
+    {
+        char* dst = static_cast<char*>(e->arenaPool) + off;
+        err = cudaMemcpyAsync(dst, *t.first, t.second, cudaMemcpyDeviceToDevice, e->stream);
+        if (err != cudaSuccess) return err;
+        *t.first = dst;
+        off += (t.second + 255) & ~(size_t)255;
+    }
+    e->arenaPoolBytes = total;
+    size_t current = 0;
+    cudaDeviceGetLimit(&current, cudaLimitPersistingL2CacheSize);
+    if (current < total) err = cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, total);
+    return err;
+}
+
+cudaAccessPolicyWindow arenaWindow(const carlb_env* e)
+{
+    cudaAccessPolicyWindow w{};
+    w.base_ptr = e->arenaPool;
+    w.num_bytes = e->arenaPoolBytes;
+    w.hitRatio = 1.f;
+    w.hitProp = cudaAccessPropertyPersisting;
+    w.missProp = cudaAccessPropertyStreaming;
+    return w;
+}
+
+// Sets the arena window on every kernel node of a captured tick graph.
+cudaError_t applyArenaWindow(const carlb_env* e, cudaGraph_t graph)
+{
+    if (!e->arenaPool) return cudaSuccess;
+    size_t n = 0;
+    cudaError_t err = cudaGraphGetNodes(graph, nullptr, &n);
+    if (err != cudaSuccess) return err;
+    std::vector<cudaGraphNode_t> nodes(n);
+    err = cudaGraphGetNodes(graph, nodes.data(), &n);
+    if (err != cudaSuccess) return err;
+    cudaKernelNodeAttrValue v{};
+    v.accessPolicyWindow = arenaWindow(e);
+    for (cudaGraphNode_t node : nodes)
+    {
+        cudaGraphNodeType type;
+        if ((err = cudaGraphNodeGetType(node, &type)) != cudaSuccess) return err;
+        if (type != cudaGraphNodeTypeKernel) continue;
+        if ((err = cudaGraphKernelNodeSetAttribute(node, cudaKernelNodeAttributeAccessPolicyWindow, &v)) != cudaSuccess)
+            return err;
+    }
+    return cudaSuccess;
+}
+
 size_t actionRowBytes(carlb_action_kind kind) { return kind == CARLB_ACTIONS_DIRECT ? 32 : 28; }
 
 // hostIn: the actions are being copied in per slice on the copy stream
@@ -271,6 +354,12 @@ carlb_status launchTicks(carlb_env* e, carlb_action_kind kind, int nTicks, bool 
             {
                 if (graph) cudaGraphDestroy(graph);
                 return cudaFail(e, lerr ? (cudaError_t)lerr : cerr, "tick graph capture");
+            }
+            const cudaError_t werr = applyArenaWindow(e, graph);
+            if (werr != cudaSuccess)
+            {
+                cudaGraphDestroy(graph);
+                return cudaFail(e, werr, "tick graph access-policy window");
             }
             const cudaError_t ierr = cudaGraphInstantiate(&exec, graph, 0);
             cudaGraphDestroy(graph);
@@ -510,6 +599,7 @@ static carlb_status initEnv(carlb_env* p, const carlb_config* cfg)
         if (const char* o = std::getenv("CARLB_PHASE_OFFSET")) p->phaseOffset = std::atoi(o) != 0;
         if (const char* gr = std::getenv("CARLB_GRAPH")) p->useGraph = std::atoi(gr) != 0;
         if (const char* oc = std::getenv("CARLB_OVERLAP_COPY")) p->overlapCopy = std::atoi(oc) != 0;
+        if (const char* lw = std::getenv("CARLB_L2_WINDOW")) p->l2Window = std::atoi(lw) != 0;
         if (p->useGraph) ECHECK(p, allocZero(p, &p->tickDev, (size_t)1));
         for (int g = 0; g < p->groups; g++)
         {
@@ -640,7 +730,7 @@ static carlb_status initEnv(carlb_env* p, const carlb_config* cfg)
         }
         for (size_t e = 0; e < host->cellTris.size(); e++) cellV[3 * e + 1].w = marginN[host->cellTris[e]];
     }
-    ECHECK(p, allocZero(p, &p->cellV, cellV.size()));
+    ECHECK(p, allocArena(p, &p->cellV, cellV.size()));
     ECHECK(p, cudaMemcpyAsync(p->cellV, cellV.data(), cellV.size() * sizeof(float4), cudaMemcpyHostToDevice,
                               p->stream));
     {
@@ -648,9 +738,9 @@ static carlb_status initEnv(carlb_env* p, const carlb_config* cfg)
         for (size_t k = 0; k < bsph.size(); k++) bsph[k] = triSph[host->ballCellTris[k]];
         p->ballGrid = make_float4(host->ballOrigin[0], host->ballOrigin[1], host->ballOrigin[2], 1.f / host->ballCell);
         for (int k = 0; k < 3; k++) p->ballDims[k] = host->ballDims[k];
-        ECHECK(p, allocZero(p, &p->ballCellStart, host->ballCellStart.size()));
-        ECHECK(p, allocZero(p, &p->ballCellTris, std::max<size_t>(1, host->ballCellTris.size())));
-        ECHECK(p, allocZero(p, &p->ballCellSph, std::max<size_t>(1, bsph.size())));
+        ECHECK(p, allocArena(p, &p->ballCellStart, host->ballCellStart.size()));
+        ECHECK(p, allocArena(p, &p->ballCellTris, std::max<size_t>(1, host->ballCellTris.size())));
+        ECHECK(p, allocArena(p, &p->ballCellSph, std::max<size_t>(1, bsph.size())));
         ECHECK(p, cudaMemcpyAsync(p->ballCellStart, host->ballCellStart.data(), host->ballCellStart.size() * 4,
                                   cudaMemcpyHostToDevice, p->stream));
         ECHECK(p, cudaMemcpyAsync(p->ballCellTris, host->ballCellTris.data(), host->ballCellTris.size() * 4,
@@ -675,25 +765,39 @@ static carlb_status initEnv(carlb_env* p, const carlb_config* cfg)
             std::memcpy(&fw, &host->nativeFlags[t], 4);
             na[t] = make_float4(host->nativeAngles[3 * t], host->nativeAngles[3 * t + 1], host->nativeAngles[3 * t + 2], fw);
         }
-        ECHECK(p, allocZero(p, &p->nativeV, nv.size()));
-        ECHECK(p, allocZero(p, &p->nativeAng, na.size()));
+        ECHECK(p, allocArena(p, &p->nativeV, nv.size()));
+        ECHECK(p, allocArena(p, &p->nativeAng, na.size()));
         ECHECK(p, cudaMemcpyAsync(p->nativeV, nv.data(), nv.size() * sizeof(float4), cudaMemcpyHostToDevice, p->stream));
         ECHECK(p, cudaMemcpyAsync(p->nativeAng, na.data(), na.size() * sizeof(float4), cudaMemcpyHostToDevice,
                                   p->stream));
         ECHECK(p, cudaStreamSynchronize(p->stream));
         p->hasNative = 1;
     }
-    ECHECK(p, allocZero(p, &p->cellSph, cellSph.size()));
+    ECHECK(p, allocArena(p, &p->cellSph, cellSph.size()));
     ECHECK(p, cudaMemcpyAsync(p->cellSph, cellSph.data(), cellSph.size() * sizeof(float4), cudaMemcpyHostToDevice,
                               p->stream));
-    ECHECK(p, allocZero(p, &p->triV, triV.size()));
-    ECHECK(p, allocZero(p, &p->triAng, triAng.size()));
-    ECHECK(p, allocZero(p, &p->cellStart, host->cellStart.size()));
-    ECHECK(p, allocZero(p, &p->cellTris, host->cellTris.size()));
+    ECHECK(p, allocArena(p, &p->triV, triV.size()));
+    ECHECK(p, allocArena(p, &p->triAng, triAng.size()));
+    ECHECK(p, allocArena(p, &p->cellStart, host->cellStart.size()));
+    ECHECK(p, allocArena(p, &p->cellTris, host->cellTris.size()));
     ECHECK(p, cudaMemcpyAsync(p->triV, triV.data(), triV.size() * sizeof(float4), cudaMemcpyHostToDevice, p->stream));
     ECHECK(p, cudaMemcpyAsync(p->triAng, triAng.data(), triAng.size() * sizeof(float4), cudaMemcpyHostToDevice, p->stream));
     ECHECK(p, cudaMemcpyAsync(p->cellStart, host->cellStart.data(), host->cellStart.size() * 4, cudaMemcpyHostToDevice, p->stream));
     ECHECK(p, cudaMemcpyAsync(p->cellTris, host->cellTris.data(), host->cellTris.size() * 4, cudaMemcpyHostToDevice, p->stream));
+
+    if (p->l2Window)
+    {
+        ECHECK(p, poolArenaTables(p));
+        if (p->arenaPool)
+        {
+            cudaStreamAttrValue v{};
+            v.accessPolicyWindow = arenaWindow(p);
+            for (int g = 0; g < 8; g++)
+                for (cudaStream_t st : { p->groupStream[g], p->ballStream[g] })
+                    if (st) ECHECK(p, cudaStreamSetAttribute(st, cudaStreamAttributeAccessPolicyWindow, &v));
+            ECHECK(p, cudaStreamSetAttribute(p->stream, cudaStreamAttributeAccessPolicyWindow, &v));
+        }
+    }
 
     Tables tables;
     buildTables(tables);
