@@ -40,6 +40,28 @@ void buildTables(Tables& t)
         t.padZ[p] = pads[p].z;
         t.padBig[p] = pads[p].big;
     }
+    // Pad cell lists: every pad whose pickup disk comes within 2 uu of the cell
+    // (the margin covers a car's cell being rounded to a neighbour).  The disks
+    // are disjoint (pads are at least 1000 uu apart, radii at most 208), so a
+    // car is on at most one pad and at most 4 pads reach a cell.
+    for (int cy = 0; cy < PAD_GRID_NY; cy++)
+        for (int cx = 0; cx < PAD_GRID_NX; cx++)
+        {
+            const double x0 = PAD_GRID_X0 + (double)cx * PAD_CELL, y0 = PAD_GRID_Y0 + (double)cy * PAD_CELL;
+            unsigned word = 0xffffffffu;
+            int n = 0;
+            for (int p = 0; p < NUM_BOOST_PADS; p++)
+            {
+                const double px = pads[p].x, py = pads[p].y;
+                const double dx = px < x0 ? x0 - px : (px > x0 + PAD_CELL ? px - x0 - PAD_CELL : 0.0);
+                const double dy = py < y0 ? y0 - py : (py > y0 + PAD_CELL ? py - y0 - PAD_CELL : 0.0);
+                const double reach = (pads[p].big ? BIG_PAD_RADIUS : SMALL_PAD_RADIUS) + 2.0;
+                if (dx * dx + dy * dy >= reach * reach) continue;
+                if (n < 4) word = (word & ~(0xffu << (8 * n))) | ((unsigned)p << (8 * n));
+                n++;
+            }
+            t.padCell[cy * PAD_GRID_NX + cx] = n <= 4 ? word : 0xfffffffeu;  // 0xfffffffe: more than 4 (never)
+        }
     for (int p = 0; p < NUM_BOOST_PADS; p++)
     {
         t.padMirror[p] = p;

@@ -382,8 +382,12 @@ __device__ V3 ballArenaSolve(const SmemSoa& cars, const SmemSoa& sims, int s, in
 }
 
 // ---- ball stage, part 2: ball vs cars (in car order), integration, goal; one thread ----------
+// `gate[k]` is the distance gate of the sim's car k against the ball's
+// pre-contact position (computed by the car's own thread: a solve only moves its
+// own car and the ball, so gating each car before the first solve is the same
+// as gating it just before its own).
 __device__ void ballFinishStage(const SmemSoa& cars, const SmemSoa& sims, int s, int nCars, int tick,
-                                const float* scratch, int scratchStride)
+                                const float* scratch, int scratchStride, const unsigned char* gate)
 {
     V3 in[4];
     #pragma unroll
@@ -396,15 +400,9 @@ __device__ void ballFinishStage(const SmemSoa& cars, const SmemSoa& sims, int s,
     const V3 pushVel = in[3];
     const V3 preSolveVel = preSolveBT * 50.f;
 
-    // Distance gates use the pre-contact ball position; a solve only moves its
-    // own car and the ball, so gating each car just before its solve is the same.
     const int carBase = s * nCars;
     for (int k = 0; k < nCars; k++)
-    {
-        const int i = carBase + k;
-        if (!cars.n(C_DEMOED, i) && ballCarGate(exportedPos, cars.v(C_CEN, i)))
-            solveBallCar(cars, i, sims, s, preSolveVel, tick);
-    }
+        if (gate[k]) solveBallCar(cars, carBase + k, sims, s, preSolveVel, tick);
 
     const V3 corrected = sims.v(S_BPOS, s);
     if (lensq(corrected - exportedPos) != 0.f) posBT = corrected * .02f;
@@ -1116,8 +1114,43 @@ __global__ void __launch_bounds__(BALL_WARPS * 32) ballKernel(TickParams p, Aren
     }
 }
 
-__global__ void __launch_bounds__(FIN_THREADS) finishKernel(TickParams p, StageScratch x, int t, int simsPerBlock)
+// The boost pad whose pickup cylinder holds a car at `pos`, or -1
+// (include/Physics/BoostPads.cuh:70-106 test, same arithmetic).  The pads'
+// pickup disks are disjoint, so at most one pad holds a car; the cell list
+// narrows the pads tested to those that reach the car's cell.
+__device__ __forceinline__ int padUnderCar(V3 pos)
 {
+    const int cx = (int)floorf((pos.x - PAD_GRID_X0) * (1.f / PAD_CELL));
+    const int cy = (int)floorf((pos.y - PAD_GRID_Y0) * (1.f / PAD_CELL));
+    if (cx < 0 || cx >= PAD_GRID_NX || cy < 0 || cy >= PAD_GRID_NY) return -1;
+    const unsigned word = c_tables.padCell[cy * PAD_GRID_NX + cx];
+    const int n = word == 0xfffffffeu ? NUM_BOOST_PADS : 4;
+    for (int j = 0; j < n; j++)
+    {
+        const int pad = n == 4 ? (int)((word >> (8 * j)) & 0xffu) : j;
+        if (pad == 0xff) break;
+        const float radius = c_tables.padBig[pad] ? BIG_PAD_RADIUS : SMALL_PAD_RADIUS;
+        const float dx = pos.x - c_tables.padX[pad];
+        const float dy = pos.y - c_tables.padY[pad];
+        const float distSq = dx * dx + dy * dy;
+        if (distSq < radius * radius && fabsf(pos.z - c_tables.padZ[pad]) < BOOST_PAD_HEIGHT) return pad;
+    }
+    return -1;
+}
+
+// Finish of a CTA of `simsPerBlock` whole sims, in four phases:
+//   1. a thread per car: the car's ball gate;
+//   2. a thread per sim: ball vs its gated cars (car order), ball integration, goal;
+//   3. a thread per car: integration and finish (demo timer, respawn, outputs),
+//      then the pad under the car; a thread per sim: the ball's finish;
+//   4. a thread per (pad, sim): cooldown, and the last car (in car order) on the
+//      pad takes it (include/Physics/BoostPads.cuh:89-97).  A car is on at most
+//      one pad, so the pads of a sim are independent.
+__global__ void __launch_bounds__(FIN_THREADS, 3) finishKernel(TickParams p, StageScratch x, int t,
+                                                                int simsPerBlock)
+{
+    __shared__ unsigned char gateS[FIN_THREADS];
+    __shared__ signed char padS[FIN_THREADS];
     const int tid = threadIdx.x;
     const int nCars = p.nCars;
     const int s0 = blockIdx.x * simsPerBlock;
@@ -1139,7 +1172,16 @@ __global__ void __launch_bounds__(FIN_THREADS) finishKernel(TickParams p, StageS
         *x.ccCount = 0;
         for (int c = 0; c < HEAVY_CLASSES; c++) x.heavyCount[c] = 0;
     }
-    if (tid < simsHere) ballFinishStage(cars, sims, s0 + tid, nCars, tick, x.ball, (int)p.simStride);
+    if (tid < carsHere)
+    {
+        const int i = s0 * nCars + tid;
+        const int s = s0 + tid / nCars;
+        const V3 exportedPos{ x.ball[0 * p.simStride + s], x.ball[1 * p.simStride + s], x.ball[2 * p.simStride + s] };
+        gateS[tid] = !cars.n(C_DEMOED, i) && ballCarGate(exportedPos, cars.v(C_CEN, i));
+    }
+    __syncthreads();
+    if (tid < simsHere)
+        ballFinishStage(cars, sims, s0 + tid, nCars, tick, x.ball, (int)p.simStride, gateS + tid * nCars);
     __syncthreads();
     if (tid < carsHere)
     {
@@ -1158,6 +1200,7 @@ __global__ void __launch_bounds__(FIN_THREADS) finishKernel(TickParams p, StageS
         }
         const Controls ctl = decodeAction(p.actions, p.actionKind, i);
         const bool respawned = finishCar(cars, i, ctl.steer, (i % nCars) >= p.nBlue, c_tables);
+        padS[tid] = cars.n(C_DEMOED, i) ? -1 : (signed char)padUnderCar(cars.v(C_POS, i));
         if (lastTick)
         {
             const unsigned bits = x.wheelBits[i];
@@ -1180,8 +1223,24 @@ __global__ void __launch_bounds__(FIN_THREADS) finishKernel(TickParams p, StageS
     for (int it = tid; it < simsHere * NUM_BOOST_PADS; it += blockDim.x)
     {
         const int pad = it / simsHere;
-        const int s = s0 + (it - pad * simsHere);
-        boostPad(cars, s * nCars, nCars, sims, s, pad, c_tables);
+        const int ls = it - pad * simsHere;
+        const int s = s0 + ls;
+        float cd = sims.f(S_PADS + pad, s);
+        if (cd > 0.f)
+        {
+            cd = fmaxf(cd - PHYS_DT, 0.f);
+            sims.f(S_PADS + pad, s) = cd;
+        }
+        if (cd > 0.f) continue;
+        int locked = -1;
+        for (int k = 0; k < nCars; k++)
+            if (padS[ls * nCars + k] == pad) locked = s * nCars + k;
+        if (locked < 0) continue;
+        const bool big = c_tables.padBig[pad] != 0;
+        const float boost = cars.f(C_INT + I_BOOST, locked);
+        if (boost >= BOOST_MAX) continue;
+        cars.f(C_INT + I_BOOST, locked) = fminf(boost + (big ? BIG_PAD_AMOUNT : SMALL_PAD_AMOUNT), BOOST_MAX);
+        sims.f(S_PADS + pad, s) = big ? BIG_PAD_COOLDOWN : SMALL_PAD_COOLDOWN;
     }
 }
 
