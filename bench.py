@@ -70,11 +70,13 @@ BYTES_PER_SIM_TICK = 504
 #   flat      pose in (pos, vel, ang, cen, rot: 16 words), candidate list start,
 #             count, SAT hit mask (9 words) and ray keys (8 words) out, episode
 #             tick read-modify-write per sim.
-#   rayCtl    pose, keys, controls state in (74 words), rays, wheel bits and
-#             controls state out (62 words), ball position per sim.
-#   susp      hits, rays, body, suspension, friction and manifold state in
-#             (70 words), suspension state, friction and velocities out
-#             (33 words).
+#   ray       own pose (centre, rotation: 7 words), demolition flag, ray keys (8
+#             words) and candidate start in, rays (16 words) and wheel bits out;
+#             ball position per sim.
+#   ctlSusp   controls and suspension: actions (8), control state (24), staging
+#             (15), velocities, rays, body, friction and manifold state, SAT hit
+#             words in (about 102 words); control state, staging, friction and
+#             velocities or the contact hand-over out (about 60 words).
 #   contact   per listed car: hand-over velocities (18 words), pose, candidate
 #             range and hit mask in (20 words), pose, velocities and manifold
 #             count and normal out (20 words).
@@ -94,8 +96,8 @@ STAGE_BYTES = {
     # stage: (bytes per car, bytes per sim, {work list: bytes per entry})
     "ballPrep": (0, 148, {}),
     "flat": (140, 8, {}),
-    "rayCtl": (544, 12, {}),
-    "susp": (412, 0, {}),
+    "ray": (136, 12, {}),
+    "ctlSusp": (648, 0, {}),
     "contact": (0, 0, {"plane_cars": 232, "sat_cars": 232}),
     "carCar": (16, 0, {"car_car_sims_cars": 192}),
     "ball": (0, 0, {"moving_balls": 144}),

@@ -309,7 +309,7 @@ class Env:
         self._check(self._lib.carlb_last_tick_ms(self._h, ctypes.byref(ms)))
         return ms.value
 
-    STAGES = ["ballPrep", "flat", "rayCtl", "susp", "contact", "carCar", "ball", "finish"]
+    STAGES = ["ballPrep", "flat", "ray", "ctlSusp", "contact", "carCar", "ball", "finish"]
 
     def set_stage_timing(self, enabled: bool) -> None:
         self._check(self._lib.carlb_set_stage_timing(self._h, int(enabled)))

@@ -423,8 +423,8 @@ __device__ void ballFinishStage(const SmemSoa& cars, const SmemSoa& sims, int s,
 // =========================================================================================
 // Stage kernels, per tick and sim slice:
 //   flatKernel     begin step, broadphase, (car, candidate) wheel rays + SAT, per CTA of cars
-//   rayCtlKernel   ray finish (arena hit, other cars' boxes, ball), controls
-//   suspKernel     suspension; cars that may touch a plane or the mesh are listed
+//   rayKernel      ray finish (arena hit, other cars' boxes, ball)
+//   ctlSuspKernel  controls, then suspension; cars that may touch a plane or the mesh are listed
 //   contactKernel  plane + mesh manifold and car-arena solve of the listed cars
 //   ballPrepKernel ball prelude (moving balls are listed)
 //   carCarKernel   car-car pairs per sim
@@ -439,8 +439,8 @@ __global__ void setTickKernel(int* dst, int value) { *dst = value; }
 
 constexpr int CAND_BLOCK = 128;   // cars per candKernel CTA (car numbers fit the uint8 item map)
 constexpr int CAND_MAP_CAP = 12288;  // items per CTA resolved through the shared item -> car map
-constexpr int RAY_BLOCK = 128;    // cars per rayCtlKernel CTA
-constexpr int SOLVE_BLOCK = 128;  // cars per suspKernel / contactKernel CTA
+constexpr int RAY_BLOCK = 128;    // cars per rayKernel CTA
+constexpr int SOLVE_BLOCK = 128;  // cars per ctlSuspKernel / contactKernel CTA
 constexpr int CC_BLOCK = 128;     // sims per carCarKernel CTA
 constexpr int BALL_WARPS = 4;     // sims (warps) per ballKernel CTA
 constexpr int FIN_THREADS = 256;  // threads per finishKernel CTA
@@ -652,7 +652,10 @@ __global__ void __launch_bounds__(CAND_BLOCK) flatKernel(TickParams p, ArenaDev 
     for (int w = 0; w < NUM_WHEELS; w++) x.keys[(long long)w * p.carStride + i] = keyS[w * B + tid];
 }
 
-__global__ void __launch_bounds__(RAY_BLOCK) rayCtlKernel(TickParams p, ArenaDev arena, StageScratch x, int t)
+// Wheel rays of a car: the arena hit found by the flat stage, then the other
+// cars' boxes (car order) and the ball.  No control state is touched here, so
+// the kernel needs few registers and a slice runs in one wave.
+__global__ void __launch_bounds__(RAY_BLOCK) rayKernel(TickParams p, ArenaDev arena, StageScratch x, int t)
 {
     const int n = p.nSim * p.nCars;
     const int i = blockIdx.x * RAY_BLOCK + threadIdx.x;
@@ -790,20 +793,12 @@ __global__ void __launch_bounds__(RAY_BLOCK) rayCtlKernel(TickParams p, ArenaDev
         }
     }
 
-    // Controls.
-    const Controls ctl = decodeAction(p.actions, p.actionKind, i);
-    V3 vel = cars.v(C_VEL, i), ang = cars.v(C_ANG, i);
-    Internal st = loadInternal(cars, i);
-    Susp su = loadSusp(cars, i);
-    processControls(ctl, cars.n(C_DEMOED, i) != 0, rot, vel, ang, st, su, rayDist, cars.n(C_MAN_COUNT, i),
-                    cars.v(C_MAN_N0, i));
-    cars.setv(C_VEL, i, vel);
-    cars.setv(C_ANG, i, ang);
-    storeInternal(cars, i, st);
-    storeSusp(cars, i, su);
 }
 
-__global__ void __launch_bounds__(SOLVE_BLOCK) suspKernel(TickParams p, ArenaDev arena, StageScratch x, int t)
+// Controls and suspension of a car, one thread each: the control state machine's
+// outputs (velocities, suspension staging) feed the suspension in registers.
+// Capped at 168 registers (3 CTAs per SM; 16 bytes spilled).
+__global__ void __launch_bounds__(SOLVE_BLOCK, 3) ctlSuspKernel(TickParams p, ArenaDev arena, StageScratch x, int t)
 {
     const int n = p.nSim * p.nCars;
     const int i = blockIdx.x * SOLVE_BLOCK + threadIdx.x;
@@ -829,19 +824,34 @@ __global__ void __launch_bounds__(SOLVE_BLOCK) suspKernel(TickParams p, ArenaDev
         p.diagCar[2 * p.carStride + i] = nh;
         for (int r = nh; r < MAX_CAR_TRI_PAIRS; r++) p.diagCar[(3 + r) * p.carStride + i] = -1;
     }
-    if (cars.n(C_DEMOED, i)) return;
-
+    // Controls (the ray stage has finished the wheel rays).
     float rayDist[NUM_WHEELS];
+    #pragma unroll
+    for (int w = 0; w < NUM_WHEELS; w++) rayDist[w] = x.ray[(long long)w * p.carStride + i];
+    const bool demoed = cars.n(C_DEMOED, i) != 0;
+    Susp su = loadSusp(cars, i);
+    V3 velC = cars.v(C_VEL, i), angC = cars.v(C_ANG, i);
+    {
+        const Controls ctl = decodeAction(p.actions, p.actionKind, i);
+        Internal st = loadInternal(cars, i);
+        processControls(ctl, demoed, cars.q(C_ROT, i), velC, angC, st, su, rayDist, cars.n(C_MAN_COUNT, i),
+                        cars.v(C_MAN_N0, i));
+        storeInternal(cars, i, st);
+    }
+    if (demoed)
+    {
+        cars.setv(C_VEL, i, velC);
+        cars.setv(C_ANG, i, angC);
+        storeSusp(cars, i, su);
+        return;
+    }
+
     V3 rayNormal[NUM_WHEELS];
     #pragma unroll
     for (int w = 0; w < NUM_WHEELS; w++)
-    {
-        rayDist[w] = x.ray[(long long)w * p.carStride + i];
         rayNormal[w] = V3{ x.ray[(long long)(4 + 3 * w) * p.carStride + i], x.ray[(long long)(5 + 3 * w) * p.carStride + i],
                            x.ray[(long long)(6 + 3 * w) * p.carStride + i] };
-    }
-    Body body = loadCarBody(cars, i);
-    Susp su = loadSusp(cars, i);
+    Body body = makeBody(cars.v(C_POS, i), velC, angC, cars.v(C_CEN, i), cars.q(C_ROT, i));
     float lat[NUM_WHEELS], lon[NUM_WHEELS];
     #pragma unroll
     for (int w = 0; w < NUM_WHEELS; w++)
@@ -882,7 +892,7 @@ __global__ void __launch_bounds__(SOLVE_BLOCK) suspKernel(TickParams p, ArenaDev
     cars.setv(C_ANG, i, body.ang + body.extAng + body.deltaAng);
 }
 
-// Velocities after the suspension of a listed car (from suspKernel).
+// Velocities after the suspension of a listed car (from ctlSuspKernel).
 __device__ __forceinline__ Body loadHeavyBody(const CarSoa& cars, const StageScratch& x, long long stride, int i)
 {
     Body body = loadCarBody(cars, i);
@@ -1278,8 +1288,8 @@ int staticScratchAddress(void** ptr, size_t* bytes, void** lastUse)
         // stage's shared-memory opt-in, now: with lazy module loading a kernel's
         // first launch would otherwise load its code and may allocate device
         // memory inside a call that promises to allocate nothing.
-        const void* kernels[] = { (const void*)ballPrepKernel, (const void*)flatKernel, (const void*)rayCtlKernel,
-                                  (const void*)suspKernel, (const void*)contactKernel, (const void*)carCarKernel,
+        const void* kernels[] = { (const void*)ballPrepKernel, (const void*)flatKernel, (const void*)rayKernel,
+                                  (const void*)ctlSuspKernel, (const void*)contactKernel, (const void*)carCarKernel,
                                   (const void*)ballKernel, (const void*)finishKernel };
         for (const void* k : kernels)
         {
@@ -1465,10 +1475,10 @@ int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch&
                     return (int)err;
             }
             mark(2, false, sq);
-            rayCtlKernel<<<(n + RAY_BLOCK - 1) / RAY_BLOCK, RAY_BLOCK, 0, sq>>>(q, a, y, t);
+            rayKernel<<<(n + RAY_BLOCK - 1) / RAY_BLOCK, RAY_BLOCK, 0, sq>>>(q, a, y, t);
             mark(2, true, sq);
             mark(3, false, sq);
-            suspKernel<<<(n + SOLVE_BLOCK - 1) / SOLVE_BLOCK, SOLVE_BLOCK, 0, sq>>>(q, a, y, t);
+            ctlSuspKernel<<<(n + SOLVE_BLOCK - 1) / SOLVE_BLOCK, SOLVE_BLOCK, 0, sq>>>(q, a, y, t);
             mark(3, true, sq);
             if (nG > 1 && aux.wideDone[0] && (err = cudaEventRecord((cudaEvent_t)aux.wideDone[g], sq)) != cudaSuccess)
                 return (int)err;

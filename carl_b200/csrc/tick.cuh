@@ -88,7 +88,7 @@ constexpr int HEAVY_CLASSES = 2;
 constexpr int STAGE_WORK = 4;
 
 // Stage kernels of one tick of the staged path, in launch order:
-// ballPrep, flat, rayCtl, susp, contact, carCar, ball, finish.
+// ballPrep, flat, ray, ctlSusp (controls + suspension), contact, carCar, ball, finish.
 constexpr int STAGE_KERNELS = 8;
 
 // Streams and events of the staged path (cudaStream_t / cudaEvent_t): the sims

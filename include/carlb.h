@@ -313,7 +313,7 @@ carlb_status carlb_last_tick_ms(const carlb_env* env, float* ms);
  * stream).  No counterpart in the reference (profiling aid). */
 carlb_status carlb_set_stage_timing(carlb_env* env, int32_t enabled);
 /* Durations (ms) of the stage kernels of the last timed tick, in launch order:
- * ball prelude, candidates (flat), ray finish + controls, suspension, contact
+ * ball prelude, candidates (flat), ray finish, controls + suspension, contact
  * solve, car-car, ball arena, finish.  Waits for that tick to complete. */
 carlb_status carlb_stage_times(carlb_env* env, float* ms, int32_t capacity, int32_t* count);
 
