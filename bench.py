@@ -722,15 +722,13 @@ def run_env_workload(args, resets: bool, rank: int = 0, world: int = 1, local_ra
                 current.wait_stream(stream)
                 seen += obs_view[:, :, 0].sum()
                 stream.wait_stream(current)
-            elif timed:
-                e[2].record(stream)
-            if timed:
-                e[3].record(stream)
+                if timed:
+                    e[3].record(stream)
         env.synchronize()
         torch.cuda.synchronize()
         step_ms = sum(a.elapsed_time(b) for a, b, _, _ in ev) / args.steps
-        reset_ms = sum(b.elapsed_time(c) for _, b, c, _ in ev) / args.steps
-        handoff_ms = sum(c.elapsed_time(d) for _, _, c, d in ev) / args.steps
+        reset_ms = sum(b.elapsed_time(c) for _, b, c, _ in ev) / args.steps if resets else 0.0
+        handoff_ms = sum(c.elapsed_time(d) for _, _, c, d in ev) / args.steps if resets else 0.0
         t = torch.tensor([step_ms, reset_ms, handoff_ms], dtype=torch.float64, device="cuda")
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
