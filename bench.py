@@ -452,6 +452,9 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     for i in range(args.warmup):
         step(i)
     env.synchronize()
+    # The end-to-end pass replays the timed steps from this state, so both numbers
+    # cover the same steps of the trajectory.
+    snap_timed = None if args.no_e2e else env.snapshot()
 
     # ---- timed region: K steps enqueued back to back ----
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -506,10 +509,11 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     # ---- end to end through the C ABI with host buffers ----
     e2e = None
     if not args.no_e2e:
-        pinned_ctl = [torch.from_numpy(c).pin_memory() for c in host_ctl[: min(pool_n, 8)]]
+        pinned_ctl = [torch.from_numpy(c).pin_memory() for c in host_ctl]
         rewards = torch.empty(args.n_sim, dtype=torch.float32).pin_memory()
-        for i in range(min(args.warmup, 3)):
-            env.ticks_host(capi.ACTIONS_DIRECT, pinned_ctl[i % len(pinned_ctl)].numpy(), TICKS_PER_STEP, rewards.numpy())
+        for i in range(min(args.warmup, 3)):  # warms the host-input graphs; the state is restored below
+            env.ticks_host(capi.ACTIONS_DIRECT, pinned_ctl[i % pool_n].numpy(), TICKS_PER_STEP, rewards.numpy())
+        env.restore(snap_timed)
         e_steps = max(1, min(args.steps, 50))
         e0 = [torch.cuda.Event(enable_timing=True) for _ in range(e_steps)]
         e1 = [torch.cuda.Event(enable_timing=True) for _ in range(e_steps)]
@@ -519,7 +523,8 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
             with torch.cuda.stream(stream):
                 flush.fill_(i & 0xFF)
                 e0[i].record(stream)
-            env.ticks_host(capi.ACTIONS_DIRECT, pinned_ctl[i % len(pinned_ctl)].numpy(), TICKS_PER_STEP, rewards.numpy())
+            env.ticks_host(capi.ACTIONS_DIRECT, pinned_ctl[(args.warmup + i) % pool_n].numpy(), TICKS_PER_STEP,
+                           rewards.numpy())
             e1[i].record(stream)
         torch.cuda.synchronize()
         barrier()
@@ -528,7 +533,8 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
             dist.all_reduce(ems, op=dist.ReduceOp.MAX)
         e2e = {"value": n_total_cars * TICKS_PER_STEP * e_steps * world / (float(ems[0]) / 1e3), "unit": UNIT,
                "h2d_bytes_per_step": int(host_ctl[0].nbytes), "d2h_bytes_per_step": int(rewards.numel() * 4),
-               "steps": e_steps, "path": "carlb_ticks_host (pinned host controls in, host rewards out)"}
+               "steps": e_steps, "path": "carlb_ticks_host (pinned host controls in, host rewards out)",
+               "trajectory": "the timed steps replayed from the post-warm-up state with the same controls"}
 
     if rank != 0:
         env.close()

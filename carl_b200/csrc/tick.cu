@@ -1462,9 +1462,12 @@ int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch&
             mark(1, false, sq);
             flatKernel<<<(n + CAND_BLOCK - 1) / CAND_BLOCK, CAND_BLOCK, candSmem, sq>>>(q, a, y, t);
             mark(1, true, sq);
+            mark(2, false, sq);
+            rayKernel<<<(n + RAY_BLOCK - 1) / RAY_BLOCK, RAY_BLOCK, 0, sq>>>(q, a, y, t);
+            mark(2, true, sq);
             // Actions copied in per slice beside the launch: the controls stage is the
             // first reader (the finish after it the only other), so the copy overlaps
-            // the first tick's broadphase.
+            // the first tick's broadphase and ray stages.
             if (t == 0 && aux.actionsReady[g])
             {
                 cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
@@ -1474,9 +1477,6 @@ int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch&
                                                                                    : cudaEventWaitDefault)) != cudaSuccess)
                     return (int)err;
             }
-            mark(2, false, sq);
-            rayKernel<<<(n + RAY_BLOCK - 1) / RAY_BLOCK, RAY_BLOCK, 0, sq>>>(q, a, y, t);
-            mark(2, true, sq);
             mark(3, false, sq);
             ctlSuspKernel<<<(n + SOLVE_BLOCK - 1) / SOLVE_BLOCK, SOLVE_BLOCK, 0, sq>>>(q, a, y, t);
             mark(3, true, sq);
