@@ -193,16 +193,17 @@ CB_D int clipTriToFace(const LocalTri& t, int faceAxis, V3* bufA, V3* bufB, V3**
 }
 
 // Emits the contacts of one SAT pair through `emit(const Contact&)`, in the
-// order the reference writes them.
+// order the reference writes them.  bufA and bufB hold MAX_PAIR_CONTACTS
+// vertices each: the clip polygon's storage, which the caller places in shared
+// memory (indexed by a vertex count, it would otherwise live in local memory).
 template <class Emit>
-CB_D void pairContacts(const LocalTri& t, const Sat& s, Emit&& emit)
+CB_D void pairContacts(const LocalTri& t, const Sat& s, V3* bufA, V3* bufB, Emit&& emit)
 {
     if (s.axisIdx >= 4)
     {
         emit(edgeEdgeContact(t, s.minPen, s.axisIdx, s.minAxis));
         return;
     }
-    V3 bufA[MAX_PAIR_CONTACTS], bufB[MAX_PAIR_CONTACTS];
     V3* poly;
     const int faceAxis = argMax(vabs(s.minAxis));
     const int n = clipTriToFace(t, faceAxis, bufA, bufB, &poly);
@@ -301,11 +302,16 @@ struct MPoint
     float dist;
 };
 
+// The manifold helpers index the point array only with unrolled constants (a
+// point is written to slot k where k equals its index), so a caller's MPoint[4]
+// stays in registers instead of local memory.
 CB_D bool nearManifoldPoint(const MPoint* p, int count, V3 carPos)
 {
-    for (int i = 0; i < count; i++)
-        if (lensq(p[i].carPos - carPos) < CAR_MANIFOLD_BREAK_SQ) return true;
-    return false;
+    bool near = false;
+    #pragma unroll
+    for (int i = 0; i < MAX_CAR_MANIFOLD_POINTS; i++)
+        near |= i < count && lensq(p[i].carPos - carPos) < CAR_MANIFOLD_BREAK_SQ;
+    return near;
 }
 
 CB_D int manifoldReplacement(const MPoint* p, const MPoint& cand)
@@ -327,8 +333,14 @@ CB_D int manifoldReplacement(const MPoint* p, const MPoint& cand)
     if (deepest != 2) area[2] = lensq(cross(cand.carPos - p[0].carPos, p[3].carPos - p[1].carPos));
     if (deepest != 3) area[3] = lensq(cross(cand.carPos - p[0].carPos, p[2].carPos - p[1].carPos));
     int best = 0;
+    float bestArea = area[0];
+    #pragma unroll
     for (int i = 1; i < 4; i++)
-        if (area[i] > area[best]) best = i;
+        if (area[i] > bestArea)
+        {
+            best = i;
+            bestArea = area[i];
+        }
     return best;
 }
 
@@ -337,7 +349,9 @@ CB_D void addManifoldPoint(MPoint* p, int& count, const MPoint& point)
     int idx = count;
     if (idx == MAX_CAR_MANIFOLD_POINTS) idx = manifoldReplacement(p, point);
     else count++;
-    p[idx] = point;
+    #pragma unroll
+    for (int k = 0; k < MAX_CAR_MANIFOLD_POINTS; k++)
+        if (k == idx) p[k] = point;
 }
 
 // Contacts with the floor (z = 0), ceiling (z = 2044), and side walls (x = +-4096).

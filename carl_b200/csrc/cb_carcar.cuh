@@ -122,7 +122,11 @@ CB_D Sat carCarSat(const Box& A, const Box& B)
 
 // ---- contacts ------------------------------------------------------------------------------
 
-CB_D int ccContacts(const Sat& s, const Box& A, const Box& B, CCContact* out)
+// `clip` holds 16 vertices: the two clip polygon buffers, placed by the caller in
+// shared memory (indexed by a vertex count, they would otherwise live in local
+// memory).  `out` is written only at unrolled constant slots, so the caller's
+// array stays in registers.
+CB_D int ccContacts(const Sat& s, const Box& A, const Box& B, CCContact* out, V3* clip)
 {
     if (s.axisIdx >= 6)
     {
@@ -159,7 +163,8 @@ CB_D int ccContacts(const Sat& s, const Box& A, const Box& B, CCContact* out)
     const V3 ev = boxAxis(inc, av) * vget(carHalfExtents(), av);
     const V3 center = inc.cen + incNormal * vget(carHalfExtents(), incAxis);
 
-    V3 bufA[8], bufB[8];
+    V3* bufA = clip;
+    V3* bufB = clip + 8;
     bufA[0] = center - eu - ev;
     bufA[1] = center + eu - ev;
     bufA[2] = center + eu + ev;
@@ -190,7 +195,11 @@ CB_D int ccContacts(const Sat& s, const Box& A, const Box& B, CCContact* out)
         const V3 onRef = in[i] + refNormal * depth;
         const V3 pa = refIsA ? onRef : in[i];
         const V3 pb = refIsA ? in[i] : onRef;
-        out[count++] = CCContact{ unrotate(A.rot, pa - A.cen), unrotate(B.rot, pb - B.cen), s.minAxis, fmaxf(depth, 0.f) };
+        const CCContact cc{ unrotate(A.rot, pa - A.cen), unrotate(B.rot, pb - B.cen), s.minAxis, fmaxf(depth, 0.f) };
+        #pragma unroll
+        for (int k = 0; k < MAX_CAR_MANIFOLD_POINTS; k++)
+            if (k == count) out[k] = cc;
+        count++;
     }
     if (count > 0) return count;
     out[0] = CCContact{ unrotate(A.rot, refCenter - A.cen), unrotate(B.rot, refCenter - B.cen), s.minAxis, s.minPen };
@@ -365,6 +374,7 @@ struct SimCars
     int globalBase;    // env-global index of the sim's car 0
     int tick;
     int seed;
+    V3* clip;          // this thread's clip polygon storage: 2 x 8 vertices (shared memory)
 };
 
 template <class S>
@@ -404,7 +414,7 @@ CB_D int solveCarCarPair(const SimCars<S>& sc, int ia, int ib)
     const Sat sat = carCarSat(boxA, boxB);
     if (!sat.overlap) return 0;
     CCContact contacts[MAX_CAR_MANIFOLD_POINTS];
-    const int count = ccContacts(sat, boxA, boxB, contacts);
+    const int count = ccContacts(sat, boxA, boxB, contacts, sc.clip);
     if (count == 0) return 0;
 
     // Demolition test on pre-solve state.

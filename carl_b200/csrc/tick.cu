@@ -911,11 +911,11 @@ __device__ __forceinline__ Body loadHeavyBody(const CarSoa& cars, const StageScr
 }
 
 // Manifold solve and final store of a listed car (src/Physics/CarArena/Solve.cuh order).
-// Not inlined: the contact kernel's plane-only and mesh paths share one copy of
-// the manifold solve, which keeps the kernel's code and registers smaller.  The
-// floor workloads gain (3v3 bench step 2.56-2.58 against 2.60 ms, 1v1 floor 1.71
-// against 1.76), the contact-heavy 2v2 mixed loses 2 % (3.63 against 3.55 ms).
-__device__ __noinline__ void finishContactCar(const CarSoa& cars, int i, Body& body, MPoint* pts, int cnt)
+// Inlined, so the body and the manifold stay in registers (through a call they
+// are passed in local memory, whose loads sit on the car's dependency chain).
+// With the clip polygons in shared memory, the 3v3 bench measured 869-874 M
+// agent-steps/s inlined with register manifolds against 866-870 out of line.
+__device__ __forceinline__ void finishContactCar(const CarSoa& cars, int i, Body& body, MPoint* pts, int cnt)
 {
     if (cnt > 0)
     {
@@ -952,6 +952,12 @@ __global__ void __launch_bounds__(SOLVE_BLOCK) contactKernel(TickParams p, Arena
         }
         return;
     }
+    // Each thread's two clip polygons in shared memory, an odd number of words
+    // apart, so the lanes of a warp touch distinct banks at any one vertex.
+    constexpr int CLIP_WORDS = 2 * MAX_PAIR_CONTACTS * 3 + 1;
+    __shared__ float clipS[SOLVE_BLOCK * CLIP_WORDS];
+    V3* bufA = reinterpret_cast<V3*>(clipS + threadIdx.x * CLIP_WORDS);
+    V3* bufB = bufA + MAX_PAIR_CONTACTS;
     const int HW = arena.hitWords;
     const int lane = threadIdx.x & 31;
     const int warpsPer = SOLVE_BLOCK / 32;
@@ -998,7 +1004,7 @@ __global__ void __launch_bounds__(SOLVE_BLOCK) contactKernel(TickParams p, Arena
             const LocalTri lt = localTriangle(cen, rot, V3{ q0.x, q0.y, q0.z }, V3{ q1.x, q1.y, q1.z },
                                               V3{ q2.x, q2.y, q2.z });
             const Sat sat = carTriSat(lt);
-            pairContacts(lt, sat, [&](const Contact& c) {
+            pairContacts(lt, sat, bufA, bufB, [&](const Contact& c) {
                 if (nearManifoldPoint(pts, planeCount, c.carPos)) return;
                 const float d = -c.depth;
                 if (d < bestDist)
@@ -1079,7 +1085,12 @@ __global__ void __launch_bounds__(CC_BLOCK) carCarKernel(TickParams p, StageScra
     if (tid >= nActive) return;
     const int sIdx = activeS[tid];
     const int sb = sIdx * nCars;
-    SimCars<CarSoa> sc{ cars, sb, nCars, p.nBlue, (int)(p.globalCarBase + sb), tick, p.seed };
+    // Each thread's clip polygons (16 vertices) in shared memory, an odd number of
+    // words apart: the lanes of a warp touch distinct banks at any one vertex.
+    constexpr int CC_CLIP_WORDS = 16 * 3 + 1;
+    __shared__ float ccClipS[CC_BLOCK * CC_CLIP_WORDS];
+    SimCars<CarSoa> sc{ cars, sb, nCars, p.nBlue, (int)(p.globalCarBase + sb), tick, p.seed,
+                        reinterpret_cast<V3*>(ccClipS + tid * CC_CLIP_WORDS) };
     int kept[DIAG_SIM_WORDS];
     const bool diag = lastTick && p.diagSim;
     solveCarCarSim(sc, kept, diag ? DIAG_SIM_WORDS : 0, lanes);

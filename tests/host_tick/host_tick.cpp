@@ -241,7 +241,8 @@ void HostEnv::step(const Controls* ctl)
             triVerts(tri, v0, v1, v2);
             const LocalTri lt = localTriangle(cen, rot, v0, v1, v2);
             const Sat sat = carTriSat(lt);
-            pairContacts(lt, sat, [&](const Contact& c) {
+            V3 clip[2 * MAX_PAIR_CONTACTS];
+            pairContacts(lt, sat, clip, clip + MAX_PAIR_CONTACTS, [&](const Contact& c) {
                 if (nearManifoldPoint(pts, planeCount, c.carPos)) return;
                 const float d = -c.depth;
                 if (d < bestDist) { bestDist = d; best = c; bestTri = tri; }
@@ -275,7 +276,8 @@ void HostEnv::step(const Controls* ctl)
     for (int s = 0; s < nSim; s++)
     {
         const int sb = s * nCars;
-        SimCars<SmemSoa> sc{ C, sb, nCars, nBlue, sb, tick, seed };
+        V3 clip[16];
+        SimCars<SmemSoa> sc{ C, sb, nCars, nBlue, sb, tick, seed, clip };
         int pair = 0;
         for (int a = 0; a < nCars - 1; a++)
             for (int b = a + 1; b < nCars; b++, pair++)
