@@ -10,7 +10,11 @@ pure-Python layer runs on top:
   the car and ball views) over output buffers of this project's front end,
   checked against the snapshot words those buffers were packed from;
 * its action codec (python/carl/gymnasium/action.py:17-37) over this project's
-  observations, checked against the device mask kernel's output.
+  observations, checked against the device mask kernel's output;
+* its reward context (state.py:503-515) built from this project's transition
+  state, previous state, observations, events and counters as the wrapper builds
+  it for `reward_funcs` (gymnasium/torch.py:371-418), with reward functions over
+  those views checked against the snapshot words.
 
 The buffers come from tests/golden/make_front_end_fixture.py, run on a GPU
 machine (the reference's CUDA module cannot run here and its Python sources
@@ -152,3 +156,78 @@ def test_reference_action_codec_equals_the_device_mask(ref_carl, path):
     ref_mask = codec.mask(torch.from_numpy(z["obs"])).numpy()
     assert ref_mask.shape == z["mask"].shape
     assert (ref_mask == z["mask"].astype(bool)).all()
+
+
+@pytest.mark.parametrize("path", FIXTURES, ids=[p.stem for p in FIXTURES])
+def test_reference_reward_context_over_the_drop_in(ref_carl, path):
+    """The reference's RewardContext (state.py:503-515) built from this build's
+    buffers the way its wrapper builds it for `reward_funcs`
+    (gymnasium/torch.py:371-418, whose module needs gymnasium): the transition
+    state and the previous state as CarlState, both observations, the events, the
+    actions and the transition counters.  Reward functions written against those
+    views give the values computed from the snapshot words directly."""
+    import torch
+
+    carl, state_mod, _ = ref_carl
+    z = np.load(path)
+    n_sim, nb, no, _, _, _, normalize, _ = (int(x) for x in z["dims"])
+    n_cars = nb + no
+    team_sign = torch.tensor([1.0] * nb + [-1.0] * no)
+    pads = torch.tensor(state_mod.BOOST_PAD_POSITIONS, dtype=torch.float32)
+
+    def carl_state(raw):
+        return state_mod.CarlState.from_raw(torch.from_numpy(raw), n_cars, pads, team_sign)
+
+    score_delta = torch.from_numpy(z["rewards"])
+    done = torch.from_numpy(z["dones"]).bool()
+    terminated = done & score_delta.ne(0)
+    truncated = done & ~terminated
+    ctx = state_mod.RewardContext(
+        current=carl_state(z["transition_state"]),
+        previous=carl_state(z["prev_state"]),
+        current_observation=state_mod.CARLObservation.from_tensor(torch.from_numpy(z["obs"]), n_cars),
+        previous_observation=state_mod.CARLObservation.from_tensor(torch.from_numpy(z["prev_obs"]), n_cars),
+        events=state_mod.CarlEvents(score_delta=score_delta, done=done, terminated=terminated, truncated=truncated),
+        actions=torch.from_numpy(z["actions/2"]),
+        score_difference=torch.from_numpy(z["transition_score_difference"]),
+        episode_ticks=torch.from_numpy(z["transition_episode_ticks"]),
+        overtime=torch.from_numpy(z["transition_overtime"]),
+    )
+
+    def velocity_to_ball(c):
+        to_ball = c.current.ball_position[:, None, :] - c.current.car_position
+        return (c.current.car_velocity * to_ball / to_ball.norm(dim=-1, keepdim=True)).sum(-1)
+
+    def boost_gained(c):
+        return c.current.car_boost - c.previous.car_boost
+
+    def goal(c):
+        return c.events.score_delta[:, None] * team_sign[None, :]
+
+    # The wrapper's accumulation: each function's result must be [n_sim, n_cars].
+    reward = torch.zeros((n_sim, n_cars))
+    for func in (velocity_to_ball, boost_gained, goal):
+        r = func(ctx)
+        assert r.shape == reward.shape
+        reward += r
+
+    # The same terms from the snapshot words (sims not reset by the step: there the
+    # transition state is the state after the step).
+    keep = ~z["dones"].astype(bool)
+    car_pos = _f32(z["snap/CAR_POS"]).reshape(n_sim, n_cars, 3).astype(np.float64)
+    car_vel = _f32(z["snap/CAR_VEL"]).reshape(n_sim, n_cars, 3).astype(np.float64)
+    ball_pos = _f32(z["snap/BALL_POS"]).reshape(n_sim, 1, 3).astype(np.float64)
+    to_ball = ball_pos - car_pos
+    want = (car_vel * to_ball / np.linalg.norm(to_ball, axis=-1, keepdims=True)).sum(-1)
+    want += _f32(z["snap/CAR_INTERNAL"])[:, 21].reshape(n_sim, n_cars) - \
+        _f32(z["prev_snap/CAR_INTERNAL"])[:, 21].reshape(n_sim, n_cars)
+    want += z["rewards"].astype(np.float64)[:, None] * np.array([1.0] * nb + [-1.0] * no)[None, :]
+    np.testing.assert_allclose(reward.numpy()[keep], want[keep], rtol=1e-4, atol=1e-2)
+    # The previous side is the state one step earlier, not the current one.
+    assert (ctx.previous.car_position.numpy() == _f32(z["prev_snap/CAR_POS"]).reshape(n_sim, n_cars, 3)).all()
+    assert not torch.equal(ctx.previous.car_position, ctx.current.car_position)
+    # Transition counters: the sims' episode ticks (snapshot words) and no overtime.
+    assert ctx.episode_ticks.shape == (n_sim,) and ctx.overtime.shape == (n_sim,)
+    ticks = z["snap/EPISODE_TICKS"].reshape(n_sim).astype(np.int64)
+    assert (ctx.episode_ticks.numpy()[keep] == ticks[keep]).all()
+    assert not ctx.overtime.numpy().any()
