@@ -144,17 +144,29 @@ def test_default_matches_reference_cuda_build(oracle_built, name, n_sim, nb, no,
             assert frac <= DRIFT_ROWS_8, parity.summarize(parity.compare_snapshots(a, b))
 
 
-def test_bench_size_matches_reference_cuda_build(oracle_built):
-    """The benchmark's workload at its full size: 3v3, n_sim = 32768, the seeded
-    floor states of bench.py (rank 0) after its 5 warm-up steps of 8 ticks, then
-    1 and 8 ticks of the next control set, default mode against the reference's
-    CUDA build on the same states and controls."""
+BENCH_WORKLOADS = [
+    # name, n_sim, blue, orange, initial state (bench.py initial_state, rank 0)
+    ("C3", 32768, 3, 3, "floor"),
+    ("C4", 32768, 2, 2, "mixed"),
+    ("C1", 1024, 1, 1, "kickoff"),
+]
+
+
+@pytest.mark.parametrize("name, n_sim, nb, no, state", BENCH_WORKLOADS, ids=[w[0] for w in BENCH_WORKLOADS])
+def test_bench_size_matches_reference_cuda_build(oracle_built, name, n_sim, nb, no, state):
+    """A benchmark workload at its full per-GPU size: bench.py's seeded initial
+    states (rank 0) after its 5 warm-up steps of 8 ticks, then 1 and 8 ticks of
+    the next control set, default mode against the reference's CUDA build on the
+    same states and controls."""
     from oracle.refenv import RefGpu
 
-    n_sim, nb, no, seed = 32768, 3, 3, 0
+    seed = 0
     n = n_sim * (nb + no)
     ref = RefGpu(n_sim, nb, no, seed)
-    workloads.floor_state(ref, seed)
+    if state == "kickoff":
+        ref.reset()
+    else:
+        (workloads.floor_state if state == "floor" else workloads.mixed_state)(ref, seed)
     rng = np.random.default_rng(seed + 1)
     pool = [workloads.controls(rng, n) for _ in range(6)]
     for i in range(5):
@@ -164,11 +176,11 @@ def test_bench_size_matches_reference_cuda_build(oracle_built):
     results = run_pair(n_sim, nb, no, seed, s0, pool[5], 0, RefGpu, (1, 8))
     for k, a, b, diag in results:
         if k == 1:
-            nbad = check_tick1_against_cuda_build("C3 32768", n_sim, nb + no, a, b, diag)
-            print(f"C3 n_sim=32768 tick 1: {nbad} car rows outside tolerance (all with >= 2 SAT pairs)")
+            nbad = check_tick1_against_cuda_build(f"{name} {n_sim}", n_sim, nb + no, a, b, diag)
+            print(f"{name} n_sim={n_sim} tick 1: {nbad} car rows outside tolerance (all with >= 2 SAT pairs)")
         else:
             frac = car_rows_bad(parity.compare_snapshots(a, b), n)
-            print(f"C3 n_sim=32768, 8 ticks: {100 * frac:.3f}% car rows outside tolerance")
+            print(f"{name} n_sim={n_sim}, 8 ticks: {100 * frac:.3f}% car rows outside tolerance")
             assert frac <= DRIFT_ROWS_8, parity.summarize(parity.compare_snapshots(a, b))
 
 
