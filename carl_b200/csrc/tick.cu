@@ -1426,7 +1426,12 @@ int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch&
             const StageScratch& y = gx[g];
             cudaStream_t sq = gs[g];
             const int n = q.nSim * q.nCars;
-            const int simsPerFin = FIN_THREADS / q.nCars;
+            // Sims per finish CTA: up to a CTA's threads' worth of cars, but spread over
+            // at least one wave (3 CTAs per SM) when the slice is small, so the per-sim
+            // and per-(pad, sim) phases of a small env run on many SMs (1v1, 1024 sims:
+            // 4 sims per CTA, 256 CTAs, against 128 sims in 8 CTAs).
+            const int simsPerFin = std::max(1, std::min(FIN_THREADS / q.nCars,
+                                                        std::max(4, (q.nSim + 3 * sms / nG - 1) / (3 * sms / nG))));
             const int ballBlocks = std::max(1, std::min((q.nSim + BALL_WARPS - 1) / BALL_WARPS, sms * 8 / nG));
             const int contactBlocks = std::max(1, std::min((n + SOLVE_BLOCK - 1) / SOLVE_BLOCK, sms * 2 / nG));
             const int meshBlocks = std::max(1, std::min((n + SOLVE_BLOCK - 1) / SOLVE_BLOCK, sms * 4 / nG));
