@@ -437,7 +437,8 @@ __device__ __forceinline__ int tickBase(const TickParams& p) { return p.tickDev 
 
 __global__ void setTickKernel(int* dst, int value) { *dst = value; }
 
-constexpr int CAND_BLOCK = 128;   // cars per candKernel CTA (car numbers fit the uint8 item map)
+constexpr int CAND_BLOCK = 384;   // cars per flatKernel CTA: at 78 registers, 2 CTAs (768 threads) fill an SM's
+                                  // register file; 128 and 256 measured slower (C3 880 and 898 against 905 M)
 constexpr int CAND_MAP_CAP = 12288;  // items per CTA resolved through the shared item -> car map
 constexpr int RAY_BLOCK = 128;    // cars per rayKernel CTA
 constexpr int SOLVE_BLOCK = 128;  // cars per ctlSuspKernel / contactKernel CTA
@@ -461,7 +462,7 @@ __global__ void __launch_bounds__(CAND_BLOCK) flatKernel(TickParams p, ArenaDev 
     unsigned* hitS = reinterpret_cast<unsigned*>(poseS + 7 * B);  // [HW][B]
     const size_t keyOff = ((size_t)(hitS + HW * B) - (size_t)sm + 7) & ~(size_t)7;
     unsigned long long* keyS = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(sm) + keyOff);  // [4][B]
-    unsigned char* mapS = reinterpret_cast<unsigned char*>(keyS + 4 * B);  // [CAND_MAP_CAP] item -> car
+    unsigned short* mapS = reinterpret_cast<unsigned short*>(keyS + 4 * B);  // [CAND_MAP_CAP] item -> car
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int n = p.nSim * p.nCars;
@@ -542,7 +543,7 @@ __global__ void __launch_bounds__(CAND_BLOCK) flatKernel(TickParams p, ArenaDev 
         if (tid == 0) preS[0] = 0;
         // Item -> car map for the first CAND_MAP_CAP items (later items search preS).
         const int cnt = cntS[tid];
-        for (int k = v - cnt; k < v && k < CAND_MAP_CAP; k++) mapS[k] = (unsigned char)tid;
+        for (int k = v - cnt; k < v && k < CAND_MAP_CAP; k++) mapS[k] = (unsigned short)tid;
     }
     __syncthreads();
 
@@ -1328,7 +1329,7 @@ size_t stageCandSmemBytes(int hitWords)
     const int B = CAND_BLOCK;
     size_t words = (size_t)B + B + (B + 1) + 32 + 15 * B + 7 * B + (size_t)hitWords * B;
     size_t bytes = (words * 4 + 7) & ~(size_t)7;
-    return bytes + 8 * 4 * (size_t)B + CAND_MAP_CAP;
+    return bytes + 8 * 4 * (size_t)B + 2 * CAND_MAP_CAP;
 }
 
 int stagedSetup()
@@ -1341,7 +1342,7 @@ int stagedSetup()
     std::lock_guard<std::mutex> guard(lock);
     if (dev < 0 || dev >= 64 || !configured[dev])
     {
-        err = cudaFuncSetAttribute(flatKernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+        err = cudaFuncSetAttribute(flatKernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 1024);
         if (err != cudaSuccess) return (int)err;
         if (dev >= 0 && dev < 64) configured[dev] = true;
     }
@@ -1365,7 +1366,7 @@ int launchTickStaged(const TickParams& p, const ArenaDev& a, const StageScratch&
     if (const int e = stagedSetup()) return e;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (candSmem > 64 * 1024) return (int)cudaErrorInvalidValue;
+    if (candSmem > 128 * 1024) return (int)cudaErrorInvalidValue;
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
 
