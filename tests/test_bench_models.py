@@ -42,3 +42,18 @@ def test_workload_sizes(monkeypatch, argv, blue, orange, n_sim, workload):
     args = bench.parse_args()
     assert (args.blue, args.orange, args.n_sim, args.workload) == (blue, orange, n_sim, workload)
     assert args.reset_n_sim == 131072  # C5: 1,048,576 sims over 8 GPUs
+
+
+def test_profiles_give_traffic_and_flops_for_every_stage():
+    """The roofline's per-launch DRAM traffic and FP32 work come from the committed
+    ncu summaries: every stage kernel has both, and traffic scales with the sims."""
+    import re
+
+    text = "\n".join(p.read_text() for p in sorted(bench.ROOT.joinpath("profiles").glob("*.md")))
+    for stage in bench.STAGE_BYTES:
+        t = bench.traffic_per_launch(stage, 32768)
+        assert t is not None and t > 0, stage
+        assert bench.traffic_per_launch(stage, 16384) == pytest.approx(t / 2), stage
+        assert re.search(rf"fp32_flops_per_car_tick\[{stage}\]: \d", text), stage
+    total = bench.fp32_flops_per_car_tick()
+    assert total is not None and 3000 < total < 5000
